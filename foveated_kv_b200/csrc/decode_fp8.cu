@@ -1,0 +1,668 @@
+// Fused two-tier decode attention (fp8 E4M3 K / INT4 V far tier) with spike
+// emission, split-K over the concatenated [near | far | decode] sequence and
+// the split combine done by the last CTA of each (b, kv-head, head-group).
+//
+// Semantics follow kernel foveated_2tier (csrc/kernels/foveated_attn.metal:181-432
+// of the reference): q pre-scaled by 1/sqrt(D) in fp32, near rows bounded by
+// near_valid[b,h] read once per launch, spike flag = max_far > min_near + margin
+// with the earliest far index on ties, decode-buffer scores feeding min_near.
+// Unlike the Metal kernel every (b, kv head) is read once for all its q heads
+// (GQA group on the tensor-core M dimension) and no score-gated V skip is
+// applied (the output matches dequantise-then-attend without the exp(-16) cut).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+
+#include "decode_common.cuh"
+#include "fkv_common.h"
+
+using namespace fkvdev;
+
+namespace {
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kTile = 16;
+
+struct DecodeParams {
+    const uint16_t* near_k;
+    const uint16_t* near_v;
+    const int32_t* near_valid;
+    const uint8_t* far_k;
+    const uint8_t* far_v;
+    const uint16_t* v_scale;
+    const uint16_t* v_zero;
+    const uint16_t* q;
+    const uint16_t* dec_k;
+    const uint16_t* dec_v;
+    uint16_t* out;
+    int32_t* flags;
+    int32_t* tokens;
+    float* part;          // sequence-split records (nullptr = final output)
+    int32_t* part_arg;
+    int32_t far_offset;
+    float* ws;            // split records
+    int32_t* tickets;     // one counter per (stream, head group)
+    int B, Hq, Hk, G, HG, Np, F, n_dec, dec_stride, splits, chunk;
+    float margin, qscale;
+};
+
+// record = merged state of up to 8 q heads over a token range
+template <int D>
+struct RecLayout {
+    static constexpr int M = 0, L = 8, MN = 16, MF = 24, AF = 32, O = 40;
+    static constexpr int SIZE = 40 + 8 * D;   // floats
+};
+
+template <int D>
+__device__ __forceinline__ void build_q_frags(const DecodeParams& p, int s, int hg, int lane,
+                                              uint32_t (&qa)[D / 16][4]) {
+    const int r = lane >> 2, c = lane & 3;
+    const int b = s / p.Hk, h = s % p.Hk;
+    const int g = hg * kHeadsPerTile + r;
+    constexpr int KC = D / 4;   // dims per lane chunk
+    float qv[KC];
+    if (g < p.G) {
+        const uint16_t* qrow = p.q + ((int64_t)b * p.Hq + (int64_t)h * p.G + g) * D + c * KC;
+#pragma unroll
+        for (int u = 0; u < KC / 8; ++u) {
+            const uint4 w = __ldg(reinterpret_cast<const uint4*>(qrow) + u);
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                qv[u * 8 + 2 * e] = __half2float(__ushort_as_half(ws[e] & 0xFFFF)) * p.qscale;
+                qv[u * 8 + 2 * e + 1] = __half2float(__ushort_as_half(ws[e] >> 16)) * p.qscale;
+            }
+        }
+    } else {
+#pragma unroll
+        for (int u = 0; u < KC; ++u) qv[u] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < D / 16; ++j) {
+        __half hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            hi[e] = __float2half_rn(qv[4 * j + e]);
+            lo[e] = __float2half_rn(qv[4 * j + e] - __half2float(hi[e]));
+        }
+        qa[j][0] = h2_as_u32(__halves2half2(hi[0], hi[1]));
+        qa[j][1] = h2_as_u32(__halves2half2(lo[0], lo[1]));
+        qa[j][2] = h2_as_u32(__halves2half2(hi[2], hi[3]));
+        qa[j][3] = h2_as_u32(__halves2half2(lo[2], lo[3]));
+    }
+}
+
+// ---- one 16-token tile of an fp16 segment (near tier or decode buffer) ----
+template <int D>
+__device__ __forceinline__ void fp16_tile(const uint16_t* __restrict__ kb,
+                                          const uint16_t* __restrict__ vb, int t, int end,
+                                          int lane, const uint32_t (&qa)[D / 16][4],
+                                          WarpState<D>& st) {
+    constexpr int KW = D / 8;      // u32 words per lane K chunk (D/4 halves)
+    constexpr int VW = D / 16;     // u32 words per lane V chunk (D/8 halves)
+    const int r = lane >> 2, c = lane & 3;
+    uint32_t kr[2][KW];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+        const int tok = t + 8 * n + r;
+        if (tok < end) {
+            const uint4* src = reinterpret_cast<const uint4*>(kb + (int64_t)tok * D + c * (D / 4));
+#pragma unroll
+            for (int u = 0; u < KW / 4; ++u) {
+                const uint4 w = __ldg(src + u);
+                kr[n][4 * u] = w.x; kr[n][4 * u + 1] = w.y; kr[n][4 * u + 2] = w.z; kr[n][4 * u + 3] = w.w;
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < KW; ++u) kr[n][u] = 0u;
+        }
+    }
+    uint32_t vr[4][VW];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int tok = t + (e >> 1) * 8 + 2 * c + (e & 1);
+        if (tok < end) {
+            const uint4* src = reinterpret_cast<const uint4*>(vb + (int64_t)tok * D + r * (D / 8));
+#pragma unroll
+            for (int u = 0; u < VW / 4; ++u) {
+                const uint4 w = __ldg(src + u);
+                vr[e][4 * u] = w.x; vr[e][4 * u + 1] = w.y; vr[e][4 * u + 2] = w.z; vr[e][4 * u + 3] = w.w;
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < VW; ++u) vr[e][u] = 0u;
+        }
+    }
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int j = 0; j < D / 16; ++j) {
+        mma16816(sc[0], qa[j], kr[0][2 * j], kr[0][2 * j + 1]);
+        mma16816(sc[1], qa[j], kr[1][2 * j], kr[1][2 * j + 1]);
+    }
+    float s[4], pr[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int tok = t + (j >> 1) * 8 + 2 * c + (j & 1);
+        const float v = sc[j >> 1][j & 1] + sc[j >> 1][2 + (j & 1)];
+        s[j] = tok < end ? v : -INFINITY;
+        if (tok < end) st.mn = fminf(st.mn, v);
+    }
+    st.softmax_step(s, pr, lane);
+    const uint32_t pb0 = pack_h2(pr[0], pr[1]);
+    const uint32_t pb1 = pack_h2(pr[2], pr[3]);
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+        uint32_t a[4];
+        a[0] = prmt(vr[0][i], vr[1][i], 0x5410);
+        a[1] = prmt(vr[0][i], vr[1][i], 0x7632);
+        a[2] = prmt(vr[2][i], vr[3][i], 0x5410);
+        a[3] = prmt(vr[2][i], vr[3][i], 0x7632);
+        mma16816(st.o[i], a, pb0, pb1);
+    }
+}
+
+// ---- one 16-token tile of the fp8 / INT4 far tier ----
+template <int D, int VG>
+__device__ __forceinline__ void far_tile(const DecodeParams& p, int64_t srow0, int t, int end,
+                                         int lane, const uint32_t (&qa)[D / 16][4],
+                                         WarpState<D>& st) {
+    constexpr int KW = D / 16;    // u32 words of fp8 K per lane per token (D/4 bytes)
+    constexpr int VB = D / 16;    // bytes of INT4 V per lane per token (D/8 dims)
+    const int r = lane >> 2, c = lane & 3;
+    uint32_t kr[2][KW];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+        const int tok = t + 8 * n + r;
+        if (tok < end) {
+            const uint4* src =
+                reinterpret_cast<const uint4*>(p.far_k + (srow0 + tok) * D + c * (D / 4));
+#pragma unroll
+            for (int u = 0; u < KW / 4; ++u) {
+                const uint4 w = __ldg(src + u);
+                kr[n][4 * u] = w.x; kr[n][4 * u + 1] = w.y; kr[n][4 * u + 2] = w.z; kr[n][4 * u + 3] = w.w;
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < KW; ++u) kr[n][u] = 0u;
+        }
+    }
+    uint32_t vr[4][(VB + 3) / 4];
+    uint16_t vs[4], vz[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int tok = t + (e >> 1) * 8 + 2 * c + (e & 1);
+        if (tok < end) {
+            const int64_t row = srow0 + tok;
+            const uint8_t* src = p.far_v + row * (D / 2) + r * VB;
+            if constexpr (VB == 8) {
+                const uint2 w = __ldg(reinterpret_cast<const uint2*>(src));
+                vr[e][0] = w.x;
+                vr[e][1] = w.y;
+            } else {
+                vr[e][0] = __ldg(reinterpret_cast<const uint32_t*>(src));
+            }
+            if constexpr (VG == 0) {
+                vs[e] = __ldg(p.v_scale + row);
+                vz[e] = __ldg(p.v_zero + row);
+            } else {
+                const int grp = (r * (D / 8)) / VG;
+                vs[e] = __ldg(p.v_scale + row * (D / VG) + grp);
+                vz[e] = __ldg(p.v_zero + row * (D / VG) + grp);
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < (VB + 3) / 4; ++u) vr[e][u] = 0u;
+            vs[e] = 0;
+            vz[e] = 0;
+        }
+    }
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int j = 0; j < D / 16; ++j) {
+        mma16816(sc[0], qa[j], e4m3x2_to_h2(kr[0][j]), e4m3x2_to_h2(kr[0][j] >> 16));
+        mma16816(sc[1], qa[j], e4m3x2_to_h2(kr[1][j]), e4m3x2_to_h2(kr[1][j] >> 16));
+    }
+    float s[4], pr[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int tok = t + (j >> 1) * 8 + 2 * c + (j & 1);
+        const float v = sc[j >> 1][j & 1] + sc[j >> 1][2 + (j & 1)];
+        s[j] = tok < end ? v : -INFINITY;
+        if (tok < end && v > st.mf) {
+            st.mf = v;
+            st.af = tok;
+        }
+    }
+    st.softmax_step(s, pr, lane);
+    const uint32_t pb0 = pack_h2(pr[0], pr[1]);
+    const uint32_t pb1 = pack_h2(pr[2], pr[3]);
+    const uint32_t sAB = (uint32_t)vs[0] | ((uint32_t)vs[1] << 16);
+    const uint32_t zAB = (uint32_t)vz[0] | ((uint32_t)vz[1] << 16);
+    const uint32_t sCD = (uint32_t)vs[2] | ((uint32_t)vs[3] << 16);
+    const uint32_t zCD = (uint32_t)vz[2] | ((uint32_t)vz[3] << 16);
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+        const int wi = i >> 2, bi = i & 3;
+        const uint32_t sel = (uint32_t)bi | ((uint32_t)(4 + bi) << 8);
+        const uint32_t xab = prmt(vr[0][wi], vr[1][wi], sel);
+        const uint32_t xcd = prmt(vr[2][wi], vr[3][wi], sel);
+        uint32_t a[4];
+        a[0] = dq_h2(nib2_to_h2(xab), sAB, zAB);
+        a[1] = dq_h2(nib2_to_h2(xab >> 4), sAB, zAB);
+        a[2] = dq_h2(nib2_to_h2(xcd), sCD, zCD);
+        a[3] = dq_h2(nib2_to_h2(xcd >> 4), sCD, zCD);
+        mma16816(st.o[i], a, pb0, pb1);
+    }
+}
+
+// merge `n` records (strided by `stride` floats) into the caller's registers:
+// each thread handles (head, d) pairs e = tid, tid+nthreads, ...
+template <int D>
+__device__ __forceinline__ void merge_and_emit(const DecodeParams& p, const float* recs, int n,
+                                               int stride, int s, int hg, bool from_global) {
+    using R = RecLayout<D>;
+    const int tid = threadIdx.x;
+    const int b = s / p.Hk, h = s % p.Hk;
+    auto ld = [&](const float* a) { return from_global ? __ldcg(a) : *a; };
+    for (int e = tid; e < kHeadsPerTile * D; e += kThreads) {
+        const int head = e / D, d = e % D;
+        const int g = hg * kHeadsPerTile + head;
+        if (g >= p.G) continue;
+        float M = -INFINITY;
+        for (int k = 0; k < n; ++k) M = fmaxf(M, ld(recs + k * stride + R::M + head));
+        float L = 0.f, acc = 0.f;
+        if (M != -INFINITY) {
+            for (int k = 0; k < n; ++k) {
+                const float mk = ld(recs + k * stride + R::M + head);
+                if (mk == -INFINITY) continue;
+                const float w = exp2f((mk - M) * kLog2e);
+                L = fmaf(w, ld(recs + k * stride + R::L + head), L);
+                acc = fmaf(w, ld(recs + k * stride + R::O + head * D + d), acc);
+            }
+        }
+        const int64_t bh = (int64_t)b * p.Hq + (int64_t)h * p.G + g;
+        if (p.part != nullptr) {
+            float* rec = p.part + bh * (D + 4);
+            rec[4 + d] = acc;
+            if (d == 0) {
+                float mn = INFINITY, mf = -INFINITY;
+                int af = -1;
+                for (int k = 0; k < n; ++k) {
+                    mn = fminf(mn, ld(recs + k * stride + R::MN + head));
+                    const float f = ld(recs + k * stride + R::MF + head);
+                    const float ai = ld(recs + k * stride + R::AF + head);
+                    argmax_merge(mf, af, f, __float_as_int(ai));
+                }
+                rec[0] = M;
+                rec[1] = L;
+                rec[2] = mn;
+                rec[3] = mf;
+                p.part_arg[bh] = af >= 0 ? af + p.far_offset : -1;
+            }
+        } else {
+            p.out[bh * D + d] = __half_as_ushort(__float2half_rn(L > 0.f ? acc / L : 0.f));
+            if (d == 0) {
+                float mn = INFINITY, mf = -INFINITY;
+                int af = -1;
+                for (int k = 0; k < n; ++k) {
+                    mn = fminf(mn, ld(recs + k * stride + R::MN + head));
+                    const float f = ld(recs + k * stride + R::MF + head);
+                    const float ai = ld(recs + k * stride + R::AF + head);
+                    argmax_merge(mf, af, f, __float_as_int(ai));
+                }
+                p.flags[bh] = (mf > mn + p.margin) ? 1 : 0;
+                p.tokens[bh] = af;
+            }
+        }
+    }
+}
+
+template <int D, int VG>
+__global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodeParams p) {
+    using R = RecLayout<D>;
+    __shared__ float sh_rec[kWarps * R::SIZE];   // per-warp records, then CTA record
+    __shared__ int sh_last;
+    const int split = blockIdx.x, hg = blockIdx.y, s = blockIdx.z;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int r = lane >> 2, c = lane & 3;
+
+    uint32_t qa[D / 16][4];
+    build_q_frags<D>(p, s, hg, lane, qa);
+    WarpState<D> st;
+    st.init();
+
+    const int t0 = split * p.chunk;
+    const int t1 = min(t0 + p.chunk, p.Np + p.F + p.n_dec);
+    const int nv = min(max(__ldg(p.near_valid + s), 0), p.Np);
+    int tile_base = 0;
+    // near tier [0, nv)
+    {
+        const int a = max(t0, 0), e = min(t1, nv);
+        if (a < e) {
+            const uint16_t* kb = p.near_k + (int64_t)s * p.Np * D;
+            const uint16_t* vb = p.near_v + (int64_t)s * p.Np * D;
+            const int nt = (e - a + kTile - 1) / kTile;
+            for (int i = (w - tile_base % kWarps + kWarps) % kWarps; i < nt; i += kWarps)
+                fp16_tile<D>(kb, vb, a + i * kTile, e, lane, qa, st);
+            tile_base += nt;
+        }
+    }
+    // far tier [Np, Np+F)
+    {
+        const int a = max(t0, p.Np) - p.Np, e = min(t1, p.Np + p.F) - p.Np;
+        if (a < e) {
+            const int nt = (e - a + kTile - 1) / kTile;
+            const int64_t srow0 = (int64_t)s * p.F;
+            for (int i = (w - tile_base % kWarps + kWarps) % kWarps; i < nt; i += kWarps)
+                far_tile<D, VG>(p, srow0, a + i * kTile, e, lane, qa, st);
+            tile_base += nt;
+        }
+    }
+    // decode buffer [Np+F, Np+F+n_dec)
+    {
+        const int base = p.Np + p.F;
+        const int a = max(t0, base) - base, e = min(t1, base + p.n_dec) - base;
+        if (a < e) {
+            const uint16_t* kb = p.dec_k + (int64_t)s * p.dec_stride * D;
+            const uint16_t* vb = p.dec_v + (int64_t)s * p.dec_stride * D;
+            const int nt = (e - a + kTile - 1) / kTile;
+            for (int i = (w - tile_base % kWarps + kWarps) % kWarps; i < nt; i += kWarps)
+                fp16_tile<D>(kb, vb, a + i * kTile, e, lane, qa, st);
+            tile_base += nt;
+        }
+    }
+
+    // ---- warp record -> shared memory
+    st.l = quad_sum(st.l);
+    st.mn = quad_min(st.mn);
+    quad_argmax(st.mf, st.af);
+    float* wr = sh_rec + w * R::SIZE;
+    if (c == 0) {
+        wr[R::M + r] = st.m;
+        wr[R::L + r] = st.l;
+        wr[R::MN + r] = st.mn;
+        wr[R::MF + r] = st.mf;
+        wr[R::AF + r] = __int_as_float(st.af);
+    }
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+        const int d0 = r * (D / 8) + 2 * i;
+        wr[R::O + (2 * c) * D + d0] = st.o[i][0];
+        wr[R::O + (2 * c + 1) * D + d0] = st.o[i][1];
+        wr[R::O + (2 * c) * D + d0 + 1] = st.o[i][2];
+        wr[R::O + (2 * c + 1) * D + d0 + 1] = st.o[i][3];
+    }
+    __syncthreads();
+
+    if (p.splits == 1) {
+        merge_and_emit<D>(p, sh_rec, kWarps, R::SIZE, s, hg, false);
+        return;
+    }
+
+    // ---- CTA record -> workspace, then the last CTA of this stream merges
+    const int64_t slot = ((int64_t)s * p.HG + hg) * p.splits + split;
+    float* gr = p.ws + slot * R::SIZE;
+    for (int e = threadIdx.x; e < 8 * D + 8; e += kThreads) {
+        if (e < 8 * D) {
+            const int head = e / D;
+            float M = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < kWarps; ++k) M = fmaxf(M, sh_rec[k * R::SIZE + R::M + head]);
+            float acc = 0.f;
+            if (M != -INFINITY) {
+#pragma unroll
+                for (int k = 0; k < kWarps; ++k) {
+                    const float mk = sh_rec[k * R::SIZE + R::M + head];
+                    if (mk != -INFINITY)
+                        acc = fmaf(exp2f((mk - M) * kLog2e), sh_rec[k * R::SIZE + R::O + e], acc);
+                }
+            }
+            gr[R::O + e] = acc;
+        } else {
+            const int head = e - 8 * D;
+            float M = -INFINITY, L = 0.f, mn = INFINITY, mf = -INFINITY;
+            int af = -1;
+#pragma unroll
+            for (int k = 0; k < kWarps; ++k) M = fmaxf(M, sh_rec[k * R::SIZE + R::M + head]);
+#pragma unroll
+            for (int k = 0; k < kWarps; ++k) {
+                const float* q = sh_rec + k * R::SIZE;
+                if (q[R::M + head] != -INFINITY)
+                    L = fmaf(exp2f((q[R::M + head] - M) * kLog2e), q[R::L + head], L);
+                mn = fminf(mn, q[R::MN + head]);
+                argmax_merge(mf, af, q[R::MF + head], __float_as_int(q[R::AF + head]));
+            }
+            gr[R::M + head] = M;
+            gr[R::L + head] = L;
+            gr[R::MN + head] = mn;
+            gr[R::MF + head] = mf;
+            gr[R::AF + head] = __int_as_float(af);
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int* tk = p.tickets + ((int64_t)s * p.HG + hg);
+        const int old = atomicAdd(tk, 1);
+        sh_last = (old == p.splits - 1);
+        if (sh_last) *tk = 0;   // every other CTA of this stream has arrived
+    }
+    __syncthreads();
+    if (!sh_last) return;
+    __threadfence();
+    const float* base = p.ws + ((int64_t)s * p.HG + hg) * p.splits * R::SIZE;
+    merge_and_emit<D>(p, base, p.splits, R::SIZE, s, hg, true);
+}
+
+template <int D>
+__global__ void combine_kernel(int P, int N, const float* __restrict__ parts,
+                               const int32_t* __restrict__ args, float margin,
+                               uint16_t* __restrict__ out, int32_t* __restrict__ flags,
+                               int32_t* __restrict__ tokens) {
+    const int n = blockIdx.x;
+    const int64_t rs = D + 4;
+    float M = -INFINITY;
+    for (int k = 0; k < P; ++k) M = fmaxf(M, parts[((int64_t)k * N + n) * rs]);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        float L = 0.f, acc = 0.f;
+        if (M != -INFINITY) {
+            for (int k = 0; k < P; ++k) {
+                const float* rec = parts + ((int64_t)k * N + n) * rs;
+                if (rec[0] == -INFINITY) continue;
+                const float wgt = exp2f((rec[0] - M) * kLog2e);
+                L = fmaf(wgt, rec[1], L);
+                acc = fmaf(wgt, rec[4 + d], acc);
+            }
+        }
+        out[(int64_t)n * D + d] = __half_as_ushort(__float2half_rn(L > 0.f ? acc / L : 0.f));
+    }
+    if (threadIdx.x == 0) {
+        float mn = INFINITY, mf = -INFINITY;
+        int af = -1;
+        for (int k = 0; k < P; ++k) {
+            const float* rec = parts + ((int64_t)k * N + n) * rs;
+            mn = fminf(mn, rec[2]);
+            if (rec[3] > mf) {   // shard order: first shard with the strict max wins
+                mf = rec[3];
+                af = args[(int64_t)k * N + n];
+            }
+        }
+        flags[n] = (mf > mn + margin) ? 1 : 0;
+        tokens[n] = af;
+    }
+}
+
+int g_num_sms = 0;
+
+int num_sms() {
+    if (g_num_sms == 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+        if (cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            g_num_sms = 148;
+    }
+    return g_num_sms;
+}
+
+struct Plan {
+    int HG, splits, chunk;
+    size_t rec_bytes, ticket_bytes;
+};
+
+Plan make_plan(const FkvDecodeShape* sh) {
+    Plan pl{};
+    const int G = sh->Hq / sh->Hk;
+    pl.HG = (G + kHeadsPerTile - 1) / kHeadsPerTile;
+    const int64_t T = (int64_t)sh->n_near_alloc + sh->n_far + sh->n_dec;
+    const int64_t streams = (int64_t)sh->B * sh->Hk * pl.HG;
+    int splits = sh->num_splits;
+    if (splits <= 0) {
+        // aim for >= 8 waves of 3 resident CTAs per SM, chunks of >= 512 tokens
+        const int64_t target = (int64_t)num_sms() * 3 * 8;
+        int64_t want = (target + streams - 1) / streams;
+        const int64_t max_by_len = std::max<int64_t>(1, (T + 511) / 512);
+        splits = (int)std::max<int64_t>(1, std::min(want, max_by_len));
+    }
+    int64_t chunk = (T + splits - 1) / splits;
+    chunk = std::max<int64_t>(kTile * kWarps, (chunk + kTile * kWarps - 1) / (kTile * kWarps) * (kTile * kWarps));
+    pl.splits = (int)std::max<int64_t>(1, (T + chunk - 1) / chunk);
+    pl.chunk = (int)chunk;
+    const int D = sh->D;
+    pl.rec_bytes = pl.splits > 1 ? (size_t)streams * pl.splits * (40 + 8 * D) * sizeof(float) : 0;
+    pl.ticket_bytes = (size_t)streams * sizeof(int32_t);
+    return pl;
+}
+
+int validate(const FkvDecodeShape* sh) {
+    FKV_REQUIRE(sh != nullptr, FKV_ERR_INVALID, "decode shape is NULL");
+    FKV_REQUIRE(sh->B > 0 && sh->Hq > 0 && sh->Hk > 0, FKV_ERR_INVALID,
+                "B=%d Hq=%d Hk=%d must be positive", sh->B, sh->Hq, sh->Hk);
+    FKV_REQUIRE(sh->Hq % sh->Hk == 0, FKV_ERR_INVALID, "Hq=%d not a multiple of Hk=%d", sh->Hq,
+                sh->Hk);
+    FKV_REQUIRE(sh->D == 64 || sh->D == 128, FKV_ERR_UNSUPPORTED,
+                "head dim %d unsupported (64, 128)", sh->D);
+    FKV_REQUIRE(sh->n_near_alloc >= 0 && sh->n_far >= 0 && sh->n_dec >= 0 &&
+                    sh->dec_stride >= sh->n_dec,
+                FKV_ERR_INVALID, "bad tier sizes Np=%d F=%d n_dec=%d dec_stride=%d",
+                sh->n_near_alloc, sh->n_far, sh->n_dec, sh->dec_stride);
+    FKV_REQUIRE((int64_t)sh->B * sh->Hk <= 65535, FKV_ERR_UNSUPPORTED,
+                "B*Hk=%lld exceeds the grid limit 65535", (long long)sh->B * sh->Hk);
+    return FKV_OK;
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws_bytes,
+           cudaStream_t st) {
+    const Plan pl = make_plan(sh);
+    const size_t need = pl.rec_bytes + pl.ticket_bytes;
+    FKV_REQUIRE(workspace != nullptr && ws_bytes >= need, FKV_ERR_INVALID,
+                "workspace too small: %zu < %zu bytes", ws_bytes, need);
+    FKV_REQUIRE(aligned16(workspace), FKV_ERR_INVALID, "workspace must be 16-byte aligned");
+    p.B = sh->B; p.Hq = sh->Hq; p.Hk = sh->Hk; p.G = sh->Hq / sh->Hk; p.HG = pl.HG;
+    p.Np = sh->n_near_alloc; p.F = sh->n_far; p.n_dec = sh->n_dec; p.dec_stride = sh->dec_stride;
+    p.splits = pl.splits; p.chunk = pl.chunk; p.margin = sh->spike_margin;
+    p.qscale = (float)(1.0 / sqrt((double)sh->D));   // same f32 constant as the host oracle
+    p.ws = reinterpret_cast<float*>(workspace);
+    p.tickets = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(workspace) + pl.rec_bytes);
+    dim3 grid(pl.splits, pl.HG, sh->B * sh->Hk);
+    if (sh->D == 128) {
+        if (sh->v_group == 0) decode_fp8_kernel<128, 0><<<grid, kThreads, 0, st>>>(p);
+        else decode_fp8_kernel<128, 32><<<grid, kThreads, 0, st>>>(p);
+    } else {
+        if (sh->v_group == 0) decode_fp8_kernel<64, 0><<<grid, kThreads, 0, st>>>(p);
+        else decode_fp8_kernel<64, 32><<<grid, kThreads, 0, st>>>(p);
+    }
+    FKV_LAUNCH_CHECK();
+    return FKV_OK;
+}
+
+int fill_common(const FkvDecodeShape* sh, DecodeParams& p, const uint16_t* near_k,
+                const uint16_t* near_v, const int32_t* near_valid, const uint8_t* far_k,
+                const uint8_t* far_v, const uint16_t* v_scale, const uint16_t* v_zero,
+                const uint16_t* q, const uint16_t* dec_k, const uint16_t* dec_v) {
+    int rc = validate(sh);
+    if (rc) return rc;
+    FKV_REQUIRE(sh->v_group == 0 || sh->v_group == 32, FKV_ERR_UNSUPPORTED,
+                "v_group=%d unsupported (0, 32)", sh->v_group);
+    FKV_REQUIRE(q && near_valid, FKV_ERR_INVALID, "q / near_valid is NULL");
+    FKV_REQUIRE(sh->n_near_alloc == 0 || (near_k && near_v), FKV_ERR_INVALID, "near is NULL");
+    FKV_REQUIRE(sh->n_far == 0 || (far_k && far_v && v_scale && v_zero), FKV_ERR_INVALID,
+                "far tier pointer is NULL");
+    FKV_REQUIRE(sh->n_dec == 0 || (dec_k && dec_v), FKV_ERR_INVALID, "decode buffer is NULL");
+    FKV_REQUIRE(aligned16(q) && aligned16(near_k) && aligned16(near_v) && aligned16(far_k) &&
+                    aligned16(dec_k) && aligned16(dec_v) && ((uintptr_t)far_v & 3u) == 0 &&
+                    ((uintptr_t)v_scale & 1u) == 0 && ((uintptr_t)v_zero & 1u) == 0,
+                FKV_ERR_INVALID, "tier / query pointers misaligned");
+    p = DecodeParams{};
+    p.near_k = near_k; p.near_v = near_v; p.near_valid = near_valid;
+    p.far_k = far_k; p.far_v = far_v; p.v_scale = v_scale; p.v_zero = v_zero;
+    p.q = q; p.dec_k = dec_k; p.dec_v = dec_v;
+    return FKV_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s) {
+    if (validate(s) != FKV_OK) return 0;
+    const Plan pl = make_plan(s);
+    return pl.rec_bytes + pl.ticket_bytes;
+}
+
+int fkv_decode_fp8(const FkvDecodeShape* sh, const uint16_t* near_k, const uint16_t* near_v,
+                   const int32_t* near_valid, const uint8_t* far_k, const uint8_t* far_v,
+                   const uint16_t* v_scale, const uint16_t* v_zero, const uint16_t* q,
+                   const uint16_t* dec_k, const uint16_t* dec_v, uint16_t* out,
+                   int32_t* flags, int32_t* tokens, void* workspace, size_t workspace_bytes,
+                   void* stream) {
+    fkv::clear_error();
+    DecodeParams p;
+    int rc = fill_common(sh, p, near_k, near_v, near_valid, far_k, far_v, v_scale, v_zero, q,
+                         dec_k, dec_v);
+    if (rc) return rc;
+    FKV_REQUIRE(out && flags && tokens, FKV_ERR_INVALID, "outputs are NULL");
+    p.out = out; p.flags = flags; p.tokens = tokens;
+    return launch(sh, p, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int fkv_decode_fp8_partial(const FkvDecodeShape* sh, const uint16_t* near_k,
+                           const uint16_t* near_v, const int32_t* near_valid,
+                           const uint8_t* far_k, const uint8_t* far_v, const uint16_t* v_scale,
+                           const uint16_t* v_zero, const uint16_t* q, const uint16_t* dec_k,
+                           const uint16_t* dec_v, int32_t far_index_offset, float* part,
+                           int32_t* part_arg, void* workspace, size_t workspace_bytes,
+                           void* stream) {
+    fkv::clear_error();
+    DecodeParams p;
+    int rc = fill_common(sh, p, near_k, near_v, near_valid, far_k, far_v, v_scale, v_zero, q,
+                         dec_k, dec_v);
+    if (rc) return rc;
+    FKV_REQUIRE(part && part_arg, FKV_ERR_INVALID, "partial outputs are NULL");
+    p.part = part; p.part_arg = part_arg; p.far_offset = far_index_offset;
+    return launch(sh, p, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int fkv_combine_partials(int32_t P, int32_t N, int32_t D, const float* parts,
+                         const int32_t* part_args, float spike_margin, uint16_t* out,
+                         int32_t* flags, int32_t* tokens, void* stream) {
+    fkv::clear_error();
+    FKV_REQUIRE(P > 0 && N > 0, FKV_ERR_INVALID, "P=%d N=%d must be positive", P, N);
+    FKV_REQUIRE(D == 64 || D == 128, FKV_ERR_UNSUPPORTED, "head dim %d unsupported", D);
+    FKV_REQUIRE(parts && part_args && out && flags && tokens, FKV_ERR_INVALID, "NULL argument");
+    if (D == 128)
+        combine_kernel<128><<<N, 128, 0, (cudaStream_t)stream>>>(P, N, parts, part_args,
+                                                                 spike_margin, out, flags, tokens);
+    else
+        combine_kernel<64><<<N, 64, 0, (cudaStream_t)stream>>>(P, N, parts, part_args,
+                                                               spike_margin, out, flags, tokens);
+    FKV_LAUNCH_CHECK();
+    return FKV_OK;
+}
+
+}  // extern "C"

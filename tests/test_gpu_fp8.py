@@ -1,0 +1,169 @@
+"""GPU parity: fp8/INT4 compression and the fused decode kernel vs the CPU
+oracle, through libfkv.so's C ABI (via the package surface)."""
+
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fkv_oracle as O
+from foveated_kv_b200 import TierConfig, compress_layer, _native
+from foveated_kv_b200.synthetic import numpy_workload, CONFIGS
+from tests.helpers import (np_, bits, layer_to_oracle, assert_output_close,
+                           assert_spikes_match)
+
+pytestmark = pytest.mark.gpu
+
+dev = "cuda"
+
+
+def _tensors(w):
+    return {k: torch.from_numpy(v).to(dev) for k, v in w.items()}
+
+
+def _cfg_dict(cfg: TierConfig):
+    return dict(near_pct=cfg.near_pct, n_sinks=cfg.n_sinks, window_size=cfg.window_size,
+                promo_headroom_pct=cfg.promo_headroom_pct,
+                promo_headroom_min=cfg.promo_headroom_min, compress_method=cfg.compress_method,
+                select=cfg.select, v_group=cfg.v_group)
+
+
+COMPRESS_CASES = [
+    # name, B, Hk, Hq, S, D, cfg kwargs
+    ("c0_recency", 1, 2, 14, 1024, 64, dict(window_size=64)),
+    ("c0_vg32", 1, 2, 14, 1024, 64, dict(window_size=64, v_group=32)),
+    ("c1_1k", 1, 32, 32, 1024, 128, dict(window_size=128)),
+    ("b3_d128_vg32", 3, 2, 8, 300, 128, dict(window_size=16, v_group=32, near_pct=0.2)),
+    ("tiny_no_far", 1, 1, 1, 20, 64, dict()),
+    ("S1", 2, 1, 4, 1, 64, dict()),
+]
+
+
+@pytest.mark.parametrize("name,B,Hk,Hq,S,D,kw", COMPRESS_CASES)
+def test_compress_fp8_bit_exact(name, B, Hk, Hq, S, D, kw):
+    w = numpy_workload(11, B, Hk, Hq, S, D, 0)
+    cfg = TierConfig(**kw)
+    ref = O.compress_layer(w["k"], w["v"], _cfg_dict(cfg))
+    t = _tensors(w)
+    lay = compress_layer(t["k"], t["v"], cfg)
+    torch.cuda.synchronize()
+    pairs = {"near_k": lay.near_k, "near_v": lay.near_v, "near_idx": lay.near_idx,
+             "near_valid": lay.near_valid, "far_idx": lay.far_idx, "far_k": lay.far_k,
+             "far_v": lay.far_v, "far_v_scale": lay.far_v_scale, "far_v_zero": lay.far_v_zero,
+             "archive_k": lay.archive_k, "archive_v": lay.archive_v}
+    for k, tv in pairs.items():
+        a, b = bits(np_(tv)), bits(ref[k])
+        assert a.shape == b.shape, (k, a.shape, b.shape)
+        assert np.array_equal(a, b), f"{name}: {k} differs at {np.argwhere(a != b)[:5]}"
+
+
+def test_compress_golden_c0_layer(golden):
+    """Device compression reproduces the reference-generated c0 layer fixture."""
+    L = golden("layer_c0_fp8.npz")
+    c = CONFIGS["c0"]
+    w = numpy_workload(100, c["B"], c["Hk"], c["Hq"], c["S"], c["D"], c["n_dec"])
+    t = _tensors(w)
+    lay = compress_layer(t["k"], t["v"], TierConfig(window_size=64))
+    for f in ["near_k", "near_v", "near_idx", "far_k", "far_v", "far_v_scale", "far_v_zero",
+              "far_idx", "archive_k", "archive_v"]:
+        assert np.array_equal(bits(np_(getattr(lay, f))), bits(L[f])), f
+    assert np.all(np_(lay.near_valid) == L["near_valid"][None])
+
+
+DECODE_CASES = [
+    # name, B, Hk, Hq, S, D, n_dec, cfg kwargs, margin
+    ("c0_shape_dec16", 1, 2, 14, 1024, 64, 16, dict(window_size=64), 0.5),
+    ("c0_vg32", 1, 2, 14, 1024, 64, 16, dict(window_size=64, v_group=32), 0.5),
+    ("c1_1k_g1", 1, 32, 32, 1024, 128, 0, dict(window_size=128), 0.5),
+    ("g4_b2", 2, 4, 16, 2048, 128, 5, dict(), 0.5),
+    ("g8_d128", 1, 2, 16, 3000, 128, 33, dict(v_group=32), 1.0),
+    ("g16_two_head_groups", 1, 1, 16, 700, 64, 3, dict(), 0.5),
+    ("g3_ragged", 3, 3, 9, 517, 128, 7, dict(near_pct=0.25, window_size=8), 0.25),
+    ("no_far", 1, 2, 4, 30, 64, 4, dict(near_pct=0.9), 0.5),
+]
+
+
+@pytest.mark.parametrize("name,B,Hk,Hq,S,D,n_dec,kw,margin", DECODE_CASES)
+def test_decode_fp8_parity(name, B, Hk, Hq, S, D, n_dec, kw, margin):
+    w = numpy_workload(23, B, Hk, Hq, S, D, n_dec)
+    cfg = TierConfig(spike_margin=margin, **kw)
+    t = _tensors(w)
+    lay = compress_layer(t["k"], t["v"], cfg)
+    for i in range(n_dec):
+        lay.add_token(t["dec_k"][:, :, i:i + 1], t["dec_v"][:, :, i:i + 1])
+    out, flags, tokens = lay.attend_fused_with_spikes(t["q"][:, :, None, :])
+    torch.cuda.synchronize()
+    ref_lay = layer_to_oracle(lay)
+    rout, rflags, rtok, diag = O.decode_attend(ref_lay, w["q"], w["dec_k"], w["dec_v"], margin)
+    assert_output_close(np_(out).astype(np.float64)[:, :, 0], rout, name)
+    ties = assert_spikes_match(np_(flags), np_(tokens), rflags, rtok, diag, margin, name)
+    assert ties == 0
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 40])
+def test_decode_split_counts_agree(splits):
+    """Explicit split counts through the raw C ABI give the same answer."""
+    w = numpy_workload(5, 2, 2, 8, 1500, 128, 9)
+    t = _tensors(w)
+    lay = compress_layer(t["k"], t["v"], TierConfig())
+    for i in range(9):
+        lay.add_token(t["dec_k"][:, :, i:i + 1], t["dec_v"][:, :, i:i + 1])
+    lib = _native.load()
+    sh = _native.DecodeShape(B=2, Hq=8, Hk=2, D=128, n_near_alloc=lay.n_near_alloc,
+                             n_far=lay.n_far, n_dec=9, dec_stride=lay._dec_k.shape[2], v_group=0,
+                             num_splits=splits, spike_margin=0.5)
+    ws = torch.zeros(lib.fkv_decode_workspace_bytes(C.byref(sh)) + 16, dtype=torch.uint8,
+                     device=dev)
+    out = torch.empty((2, 8, 128), dtype=torch.float16, device=dev)
+    fl = torch.empty((2, 8), dtype=torch.int32, device=dev)
+    tk = torch.empty_like(fl)
+    p = lambda x: x.data_ptr()
+    for rep in range(2):   # second call reuses the workspace (counters back at zero)
+        rc = lib.fkv_decode_fp8(C.byref(sh), p(lay.near_k), p(lay.near_v), p(lay.near_valid),
+                                p(lay.far_k), p(lay.far_v), p(lay.far_v_scale),
+                                p(lay.far_v_zero), p(t["q"]), p(lay._dec_k), p(lay._dec_v),
+                                p(out), p(fl), p(tk), p(ws), ws.numel(),
+                                torch.cuda.current_stream().cuda_stream)
+        _native.check(rc, "fkv_decode_fp8")
+        torch.cuda.synchronize()
+        rout, rfl, rtk, diag = O.decode_attend(layer_to_oracle(lay), w["q"], w["dec_k"],
+                                               w["dec_v"], 0.5)
+        assert_output_close(np_(out).astype(np.float64), rout, f"splits={splits}")
+        assert assert_spikes_match(np_(fl), np_(tk), rfl, rtk, diag, 0.5) == 0
+
+
+def test_decode_per_head_near_valid():
+    """Promoted rows in headroom are attended only up to near_valid[b, h]."""
+    w = numpy_workload(9, 2, 2, 8, 800, 64, 0)
+    t = _tensors(w)
+    lay = compress_layer(t["k"], t["v"], TierConfig(spike_margin=0.5))
+    R = int(lay.near_valid[0, 0])
+    # write 3 archive rows of (b=0,h=1) and 1 row of (b=1,h=0) into headroom
+    lay.near_k[0, 1, R:R + 3] = lay.archive_k[0, 1, 10:13]
+    lay.near_v[0, 1, R:R + 3] = lay.archive_v[0, 1, 10:13]
+    lay.near_valid[0, 1] += 3
+    lay.near_k[1, 0, R] = lay.archive_k[1, 0, 0]
+    lay.near_v[1, 0, R] = lay.archive_v[1, 0, 0]
+    lay.near_valid[1, 0] += 1
+    out, fl, tk = lay.attend_fused_with_spikes(t["q"])
+    torch.cuda.synchronize()
+    rout, rfl, rtk, diag = O.decode_attend(layer_to_oracle(lay), w["q"], None, None, 0.5)
+    assert_output_close(np_(out).astype(np.float64)[:, :, 0], rout, "near_valid")
+    assert assert_spikes_match(np_(fl), np_(tk), rfl, rtk, diag, 0.5) == 0
+
+
+def test_decode_buffer_growth_and_flags_all_set():
+    """Decode buffer beyond its first capacity; margin -inf-like forces flags."""
+    w = numpy_workload(3, 1, 2, 4, 400, 128, 40)
+    t = _tensors(w)
+    lay = compress_layer(t["k"], t["v"], TierConfig(spike_margin=-1e4))
+    for i in range(40):
+        lay.add_token(t["dec_k"][:, :, i:i + 1], t["dec_v"][:, :, i:i + 1])
+    out, fl, tk = lay.attend_fused_with_spikes(t["q"])
+    torch.cuda.synchronize()
+    assert np.all(np_(fl) == 1)
+    rout, rfl, rtk, diag = O.decode_attend(layer_to_oracle(lay), w["q"], w["dec_k"], w["dec_v"],
+                                           -1e4)
+    assert_output_close(np_(out).astype(np.float64)[:, :, 0], rout, "dec40")
+    assert np.array_equal(np_(tk), rtk)
