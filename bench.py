@@ -1,0 +1,322 @@
+"""Benchmark of the fused foveated decode hot path on B200.
+
+Workload (default ``--config c3``): Llama-3-8B-shaped decode attention of one
+layer, B=64 sequences x 32 q heads / 8 KV heads x D=128 x 32K context per
+GPU, fp8 E4M3 K / per-token INT4 V far tier, 10% near tier (4 sinks, window
+32), with 1% of far tokens per (b, kv head) turned into spikes (keys set to 3
+sigma along the group's mean query) before compression.  Synthetic seeded N(0,1)
+fp16 K/V/q with 4 outlier K channels per head (there is no dataset for this
+path).  Weak scaling: each rank holds its own 64 sequences; no collective on
+the data path.
+
+One step = one fused decode launch of the layer (all 64 sequences).  Metric:
+decode tokens/s = sequences / (32 layers x per-layer time), attention only.
+``value`` uses device-resident inputs; ``e2e`` goes through the public API
+(FoveatedLayer.attend_fused_with_spikes) with the query copied from pinned
+host memory and output + spike flags/tokens read back every step.
+
+``--impl reference`` times the reference algorithm's CPU path (the NumPy
+restatement of mlx_foveated.py's dequantise-then-attend; MLX cannot run here)
+on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_LAYERS = 32          # tokens/s = B / (32 x t_layer), attention only
+METRIC = "decode attention tokens/s (B / (32 layers x per-layer fused decode time)), 1-layer c3"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c3", choices=["c3", "c1_16k", "c1_8k", "c1_4k", "c1_1k", "c0"])
+    ap.add_argument("--cpu-sample-seqs", type=int, default=1)
+    ap.add_argument("--batch", type=int, default=0, help="override sequences per GPU")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """NVML sampler of SM clock and clock-event reasons while running."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+               0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clocks_setting"}
+
+    def __init__(self, index: int, period_s: float = 0.005):
+        import pynvml
+        pynvml.nvmlInit()
+        self.nv = pynvml
+        self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+        self.period = period_s
+        self.samples = []
+        self.reasons = 0
+        self._stop = threading.Event()
+        self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self.t.join()
+
+    def summary(self):
+        rs = [n for bit, n in self.REASONS.items() if self.reasons & bit and n != "gpu_idle"]
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "samples": len(self.samples), "reasons": rs}
+
+
+def algorithmic_bytes(B, Hq, Hk, D, near_valid_sum, F, n_dec, turbo=False):
+    """Bytes one fused decode must move (each KV byte once per KV head)."""
+    far_tok = (D // 4 + D // 8 + 4 + D // 4 + 2 * (D // 32)) if turbo else (D + D // 2 + 4)
+    return (near_valid_sum * D * 4 + B * Hk * F * far_tok + B * Hk * n_dec * D * 4
+            + B * Hq * D * (2 + 2) + B * Hq * 8)
+
+
+def build_layer(cfgname, seed, device, batch=0):
+    import torch
+    from foveated_kv_b200 import TierConfig, compress_layer
+    from foveated_kv_b200.synthetic import torch_workload, CONFIGS
+    c = dict(CONFIGS[cfgname])
+    if batch:
+        c["B"] = batch
+    w = torch_workload(seed, c["B"], c["Hk"], c["Hq"], c["S"], c["D"], c["n_dec"], device)
+    cfg = TierConfig(near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
+                     v_group=c["v_group"], compress_method=c["compress_method"],
+                     spike_margin=0.5)
+    if cfgname == "c3":
+        inject_spikes(w, cfg, seed)
+    lay = compress_layer(w["k"], w["v"], cfg)
+    for i in range(c["n_dec"]):
+        lay.add_token(w["dec_k"][:, :, i:i + 1], w["dec_v"][:, :, i:i + 1])
+    q = w["q"]
+    del w
+    torch.cuda.synchronize()
+    return c, cfg, lay, q
+
+
+def inject_spikes(w, cfg, seed, frac=0.01):
+    """1% of far tokens per (b, kv head): key = 3 sigma * sqrt(D) along the
+    unit mean query of the GQA group, so they score far above min_near."""
+    import torch
+    k, q = w["k"], w["q"]
+    B, Hk, S, D = k.shape
+    G = q.shape[1] // Hk
+    tb = cfg.tier_boundaries(S)
+    F = tb["far_count"]
+    n = max(1, int(F * frac))
+    g = torch.Generator(device=k.device)
+    g.manual_seed(seed + 1)
+    pos = tb["mid_start"] + torch.randint(0, F, (B, Hk, n), generator=g, device=k.device)
+    qm = q.float().reshape(B, Hk, G, D).mean(2)
+    qm = qm / qm.norm(dim=-1, keepdim=True)
+    val = (3.0 * D ** 0.5 * qm).to(k.dtype)[:, :, None, :].expand(B, Hk, n, D)
+    k.scatter_(2, pos[..., None].expand(B, Hk, n, D), val)
+
+
+class CpuArm:
+    """The CPU oracle (dequantise-then-attend, NumPy) on `seqs` sequences of
+    the same workload; built once, timed per call."""
+
+    def __init__(self, cfgname, seqs):
+        from oracle import fkv_oracle as O
+        from foveated_kv_b200.synthetic import numpy_workload, CONFIGS
+        self.O = O
+        c = CONFIGS[cfgname]
+        self.seqs = min(seqs, c["B"])
+        self.c, self.name = c, cfgname
+        self.w = numpy_workload(7, self.seqs, c["Hk"], c["Hq"], c["S"], c["D"], c["n_dec"])
+        self.lay = O.compress_layer(self.w["k"], self.w["v"], dict(
+            near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
+            v_group=c["v_group"]))
+
+    def run(self):
+        t0 = time.perf_counter()
+        self.O.decode_attend(self.lay, self.w["q"], self.w["dec_k"], self.w["dec_v"], 0.5)
+        return time.perf_counter() - t0
+
+    def describe(self, dt):
+        cores = len(os.sched_getaffinity(0))
+        return {"value": self.seqs / (N_LAYERS * dt), "unit": "tokens/s", "cores": cores,
+                "kind": "port",
+                "sample": f"{self.seqs} of {self.c['B']} sequences of {self.name}, one layer, "
+                          f"oracle decode_attend (NumPy, BLAS threads={cores}), "
+                          f"{dt * 1e3:.1f} ms/layer"}
+
+
+def cpu_baseline(cfgname, seqs, reps=3):
+    arm = CpuArm(cfgname, seqs)
+    arm.run()
+    dt = statistics.median(arm.run() for _ in range(reps))
+    return arm.describe(dt)
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    arm = CpuArm(args.config, args.cpu_sample_seqs)
+    for _ in range(args.warmup):
+        arm.run()
+    t0 = time.perf_counter()
+    dts = [arm.run() for _ in range(args.steps)]
+    el = time.perf_counter() - t0
+    d = arm.describe(statistics.median(dts))
+    line = {"impl": "reference", "metric": METRIC, "value": d["value"], "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.config, "sample_seqs": arm.seqs},
+            "cpu_baseline": d,
+            "e2e": {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "reference CPU path = NumPy restatement of mlx_foveated.attend "
+                    "(MLX/Metal cannot run on Linux/B200)"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    from foveated_kv_b200 import _native  # noqa: F401
+
+    c, cfg, lay, q = build_layer(args.config, 1000 + rank, device, args.batch)
+    B, Hq, Hk, D = c["B"], c["Hq"], c["Hk"], c["D"]
+    st = torch.cuda.current_stream()
+    out = torch.empty((B, Hq, 1, D), dtype=torch.float16, device=device)
+
+    def step():
+        return lay.attend_fused_with_spikes(q, out=out)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(st)
+        for _ in range(args.steps):
+            step()
+        e1.record(st)
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    nv_sum = int(lay.near_valid.sum().item())
+    alg = algorithmic_bytes(B, Hq, Hk, D, nv_sum, lay.n_far, lay.n_decode,
+                            cfg.compress_method == "turbo")
+    value = world * B / (N_LAYERS * ms * 1e-3)
+
+    # ---- e2e through the public API: pinned H2D of q, D2H of out+flags+tokens
+    q_host = q.cpu().pin_memory()
+    out_h = torch.empty((B, Hq, 1, D), dtype=torch.float16).pin_memory()
+    fl_h = torch.empty((B, Hq), dtype=torch.int32).pin_memory()
+    tk_h = torch.empty((B, Hq), dtype=torch.int32).pin_memory()
+    q_dev = torch.empty_like(q)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        o, f, t = lay.attend_fused_with_spikes(q_dev)
+        out_h.copy_(o, non_blocking=True)
+        fl_h.copy_(f, non_blocking=True)
+        tk_h.copy_(t, non_blocking=True)
+        st.synchronize()
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    h2d = q.numel() * 2
+    d2h = out_h.numel() * 2 + fl_h.numel() * 4 + tk_h.numel() * 4
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.config, args.cpu_sample_seqs)
+
+    peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(peaks_path):
+        with open(peaks_path) as f:
+            peak, peak_src = json.load(f)["hbm_gbs"], "measured"
+    else:
+        peak, peak_src = 6650.0, "fallback"
+    achieved = alg / (ms * 1e-3) / 1e9
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded N(0,1) fp16, 4 outlier K channels/head, 1% spikes)",
+            "config": {"workload": args.config, "B_per_gpu": B, "Hq": Hq, "Hk": Hk, "D": D,
+                       "S": c["S"], "near_pct": c["near_pct"], "window": c["window_size"],
+                       "far_tier": "fp8 E4M3 K + per-token INT4 V",
+                       "global_batch": B * world, "parallelism": f"batch-shard x{world}",
+                       "l2": "inputs larger than L2 (no flush)"},
+            "us_per_layer": ms * 1e3, "hbm_gbs": achieved,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_src,
+                         "algorithmic_bytes_per_launch": alg, "traffic": None},
+            "e2e": {"value": world * B / (N_LAYERS * ms_e2e * 1e-3), "unit": "tokens/s",
+                    "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

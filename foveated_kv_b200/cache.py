@@ -31,20 +31,24 @@ def _stream(device=None) -> int:
 
 class _Workspace:
     """Zero-initialised scratch shared by the decode calls issued on one
-    (device, stream); calls on one stream never overlap, so sharing is safe."""
+    (device, stream); calls on one stream never overlap, so sharing is safe.
+
+    libfkv keeps split counters at the front and split records at the back of
+    the workspace, so one buffer serves every shape as long as it holds the
+    largest request seen plus the largest counter region seen (bounded here by
+    the largest request)."""
 
     _pool: dict = {}
 
     @classmethod
     def get(cls, nbytes: int, device: torch.device) -> torch.Tensor:
         key = (device.index, _stream(device))
-        buf = cls._pool.get(key)
-        if buf is None or buf.numel() < nbytes:
-            size = max(nbytes, 1 << 16)
-            if buf is not None:
-                size = max(size, 2 * buf.numel())
-            buf = torch.zeros(size, dtype=U8, device=device)
-            cls._pool[key] = buf
+        buf, peak = cls._pool.get(key, (None, 0))
+        peak = max(peak, nbytes)
+        need = 2 * peak
+        if buf is None or buf.numel() < need:
+            buf = torch.zeros(max(need, 1 << 16), dtype=U8, device=device)
+        cls._pool[key] = (buf, peak)
         return buf
 
 

@@ -559,7 +559,7 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws_bytes,
            cudaStream_t st) {
     const Plan pl = make_plan(sh);
-    const size_t need = pl.rec_bytes + pl.ticket_bytes;
+    const size_t need = pl.rec_bytes + pl.ticket_bytes + 256;
     FKV_REQUIRE(workspace != nullptr && ws_bytes >= need, FKV_ERR_INVALID,
                 "workspace too small: %zu < %zu bytes", ws_bytes, need);
     FKV_REQUIRE(aligned16(workspace), FKV_ERR_INVALID, "workspace must be 16-byte aligned");
@@ -567,8 +567,14 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     p.Np = sh->n_near_alloc; p.F = sh->n_far; p.n_dec = sh->n_dec; p.dec_stride = sh->dec_stride;
     p.splits = pl.splits; p.chunk = pl.chunk; p.margin = sh->spike_margin;
     p.qscale = (float)(1.0 / sqrt((double)sh->D));   // same f32 constant as the host oracle
-    p.ws = reinterpret_cast<float*>(workspace);
-    p.tickets = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(workspace) + pl.rec_bytes);
+    // split counters at the front, split records at the back: a workspace
+    // shared by calls of different shapes keeps every counter at zero as long
+    // as it holds the largest records region plus the largest counter region.
+    p.tickets = reinterpret_cast<int32_t*>(workspace);
+    const size_t rec_off = (ws_bytes - pl.rec_bytes) & ~(size_t)255;
+    FKV_REQUIRE(rec_off >= pl.ticket_bytes, FKV_ERR_INVALID,
+                "workspace too small for counters + records (%zu bytes)", ws_bytes);
+    p.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + rec_off);
     dim3 grid(pl.splits, pl.HG, sh->B * sh->Hk);
     if (sh->D == 128) {
         if (sh->v_group == 0) decode_fp8_kernel<128, 0><<<grid, kThreads, 0, st>>>(p);
@@ -612,7 +618,7 @@ extern "C" {
 size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s) {
     if (validate(s) != FKV_OK) return 0;
     const Plan pl = make_plan(s);
-    return pl.rec_bytes + pl.ticket_bytes;
+    return pl.rec_bytes + pl.ticket_bytes + 256;
 }
 
 int fkv_decode_fp8(const FkvDecodeShape* sh, const uint16_t* near_k, const uint16_t* near_v,

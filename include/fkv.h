@@ -132,10 +132,14 @@ typedef struct FkvDecodeShape {
     float qjl_coef;        /* turbo only: QJL term = qjl_coef/D * gamma * <sign, q S^T> */
 } FkvDecodeShape;
 
-/* Scratch bytes for fkv_decode_fp8 / fkv_decode_turbo.  The workspace must be
- * zero-filled once before first use; the kernels leave it reusable (their
- * split counters return to zero).  Calls that share a workspace must not
- * overlap on the GPU. */
+/* Scratch bytes for fkv_decode_fp8 / fkv_decode_turbo / fkv_decode_fp8_partial:
+ * split counters (4 bytes per (b, kv head, group of 8 q heads)) at the front
+ * of the workspace, split records at its back.  The workspace must be
+ * zero-filled once before first use; the kernels return the counters to zero.
+ * One workspace may serve calls of different shapes if it is at least
+ * (largest records region + largest counter region + 256) bytes, i.e. the sum
+ * of the two largest values this function returned for them.  Calls that
+ * share a workspace must not overlap on the GPU. */
 size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s);
 
 /* One fused launch per layer: near fp16 (rows [0, near_valid[b,h])) + far
