@@ -105,6 +105,7 @@ struct WarpState {
     float o[MT][4];
     float m;        // running max of head r (natural-log units)
     float l;        // partial denominator (this lane's tokens)
+    float z;        // partial sum of p * zero (per-token INT4 zero folded out of V)
     float mn;       // min near/decode score, head r
     float mf;       // max far score, head r
     int af;         // argmax far (far-local index), head r
@@ -114,6 +115,7 @@ struct WarpState {
         for (int i = 0; i < MT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
         m = -INFINITY;
         l = 0.f;
+        z = 0.f;
         mn = INFINITY;
         mf = -INFINITY;
         af = -1;
@@ -128,6 +130,7 @@ struct WarpState {
             const float mnew = up ? tmax : m;
             const float alpha = (m == -INFINITY) ? 0.f : exp2f((m - mnew) * kLog2e);
             l *= alpha;
+            z *= alpha;
             m = mnew;
             const int c = lane & 3;
             const float a0 = __shfl_sync(0xffffffffu, alpha, (2 * c) * 4);
@@ -148,5 +151,68 @@ struct WarpState {
         }
     }
 };
+
+}  // namespace fkvdev
+
+// ---------------------------------------------------------------------------
+// mbarrier + bulk-copy (TMA, non-tensor, no multicast) primitives
+// ---------------------------------------------------------------------------
+namespace fkvdev {
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of `bar` with an iteration limit; false = gave up.
+constexpr uint32_t kWaitLimit = 1u << 26;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// global -> shared bulk copy completing on `bar` (bytes and both addresses
+// multiples of 16)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
+}
 
 }  // namespace fkvdev

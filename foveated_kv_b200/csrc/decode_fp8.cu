@@ -15,6 +15,8 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <utility>
+#include <vector>
 
 #include "decode_common.cuh"
 #include "fkv_common.h"
@@ -23,8 +25,7 @@ using namespace fkvdev;
 
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
+constexpr int kThreads = 5 * 32;   // 4 consumer warps + 1 producer warp
 constexpr int kTile = 16;
 
 struct DecodeParams {
@@ -46,6 +47,7 @@ struct DecodeParams {
     int32_t far_offset;
     float* ws;            // split records
     int32_t* tickets;     // one counter per (stream, head group)
+    int32_t* status;      // sticky kernel status word (0 = ok)
     int B, Hq, Hk, G, HG, Np, F, n_dec, dec_stride, splits, chunk;
     float margin, qscale;
 };
@@ -96,10 +98,49 @@ __device__ __forceinline__ void build_q_frags(const DecodeParams& p, int s, int 
     }
 }
 
-// ---- one 16-token tile of an fp16 segment (near tier or decode buffer) ----
+// Shared-memory ring: a producer warp streams contiguous token chunks of the
+// (b, kv head) stream with bulk copies (TMA, cp.async.bulk) into kStages
+// slots; 4 consumer warps take 16-token tiles of each slot.  Slot layout:
+// [K rows | V rows]; far stages carry 128 tokens, near / decode stages 64.
+constexpr int kConsumerWarps = 4;
+constexpr int kConsumerThreads = kConsumerWarps * 32;
+constexpr int kStages = 3;
+
 template <int D>
-__device__ __forceinline__ void fp16_tile(const uint16_t* __restrict__ kb,
-                                          const uint16_t* __restrict__ vb, int t, int end,
+struct Ring {
+    static constexpr int FAR_TOK = 128;
+    static constexpr int NEAR_TOK = 64;
+    static constexpr int VOFF = NEAR_TOK * D * 2;        // K region (max of near / far)
+    static constexpr int SLOT = VOFF + NEAR_TOK * D * 2;  // + V region
+    static constexpr int BYTES = kStages * SLOT + 2 * kStages * 8;
+};
+
+struct Segs {
+    int a[3], e[3], n[3];   // tier-local [a, e) and stage counts: near, far, decode
+};
+
+template <int D>
+__device__ __forceinline__ void stage_at(const Segs& sg, int k, int& seg, int& start, int& cnt) {
+    constexpr int NT = Ring<D>::NEAR_TOK, FT = Ring<D>::FAR_TOK;
+    if (k < sg.n[0]) {
+        seg = 0;
+        start = sg.a[0] + k * NT;
+        cnt = min(NT, sg.e[0] - start);
+    } else if (k < sg.n[0] + sg.n[1]) {
+        seg = 1;
+        start = sg.a[1] + (k - sg.n[0]) * FT;
+        cnt = min(FT, sg.e[1] - start);
+    } else {
+        seg = 2;
+        start = sg.a[2] + (k - sg.n[0] - sg.n[1]) * NT;
+        cnt = min(NT, sg.e[2] - start);
+    }
+}
+
+// ---- one 16-token tile of an fp16 stage (near tier or decode buffer) ----
+template <int D>
+__device__ __forceinline__ void fp16_tile(const uint8_t* __restrict__ kbuf,
+                                          const uint8_t* __restrict__ vbuf, int u0, int cnt,
                                           int lane, const uint32_t (&qa)[D / 16][4],
                                           WarpState<D>& st) {
     constexpr int KW = D / 8;      // u32 words per lane K chunk (D/4 halves)
@@ -108,33 +149,24 @@ __device__ __forceinline__ void fp16_tile(const uint16_t* __restrict__ kb,
     uint32_t kr[2][KW];
 #pragma unroll
     for (int n = 0; n < 2; ++n) {
-        const int tok = t + 8 * n + r;
-        if (tok < end) {
-            const uint4* src = reinterpret_cast<const uint4*>(kb + (int64_t)tok * D + c * (D / 4));
+        const int u = u0 + 8 * n + r;
+        const uint4* src = reinterpret_cast<const uint4*>(kbuf + u * (2 * D) + c * (D / 2));
 #pragma unroll
-            for (int u = 0; u < KW / 4; ++u) {
-                const uint4 w = __ldg(src + u);
-                kr[n][4 * u] = w.x; kr[n][4 * u + 1] = w.y; kr[n][4 * u + 2] = w.z; kr[n][4 * u + 3] = w.w;
-            }
-        } else {
-#pragma unroll
-            for (int u = 0; u < KW; ++u) kr[n][u] = 0u;
+        for (int x = 0; x < KW / 4; ++x) {
+            const uint4 w = src[x];
+            kr[n][4 * x] = w.x; kr[n][4 * x + 1] = w.y; kr[n][4 * x + 2] = w.z; kr[n][4 * x + 3] = w.w;
         }
     }
     uint32_t vr[4][VW];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-        const int tok = t + (e >> 1) * 8 + 2 * c + (e & 1);
-        if (tok < end) {
-            const uint4* src = reinterpret_cast<const uint4*>(vb + (int64_t)tok * D + r * (D / 8));
+        const int u = u0 + (e >> 1) * 8 + 2 * c + (e & 1);
+        const bool ok = u < cnt;
+        const uint4* src = reinterpret_cast<const uint4*>(vbuf + u * (2 * D) + r * (D / 4));
 #pragma unroll
-            for (int u = 0; u < VW / 4; ++u) {
-                const uint4 w = __ldg(src + u);
-                vr[e][4 * u] = w.x; vr[e][4 * u + 1] = w.y; vr[e][4 * u + 2] = w.z; vr[e][4 * u + 3] = w.w;
-            }
-        } else {
-#pragma unroll
-            for (int u = 0; u < VW; ++u) vr[e][u] = 0u;
+        for (int x = 0; x < VW / 4; ++x) {
+            const uint4 w = ok ? src[x] : make_uint4(0, 0, 0, 0);
+            vr[e][4 * x] = w.x; vr[e][4 * x + 1] = w.y; vr[e][4 * x + 2] = w.z; vr[e][4 * x + 3] = w.w;
         }
     }
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -146,10 +178,10 @@ __device__ __forceinline__ void fp16_tile(const uint16_t* __restrict__ kb,
     float s[4], pr[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const int tok = t + (j >> 1) * 8 + 2 * c + (j & 1);
+        const int u = u0 + (j >> 1) * 8 + 2 * c + (j & 1);
         const float v = sc[j >> 1][j & 1] + sc[j >> 1][2 + (j & 1)];
-        s[j] = tok < end ? v : -INFINITY;
-        if (tok < end) st.mn = fminf(st.mn, v);
+        s[j] = u < cnt ? v : -INFINITY;
+        if (u < cnt) st.mn = fminf(st.mn, v);
     }
     st.softmax_step(s, pr, lane);
     const uint32_t pb0 = pack_h2(pr[0], pr[1]);
@@ -165,59 +197,71 @@ __device__ __forceinline__ void fp16_tile(const uint16_t* __restrict__ kb,
     }
 }
 
-// ---- one 16-token tile of the fp8 / INT4 far tier ----
+// scale/zero of the 4 V tokens a lane feeds into the PV product, packed
+// (scale | zero << 16); loaded one stage ahead from global memory
 template <int D, int VG>
-__device__ __forceinline__ void far_tile(const DecodeParams& p, int64_t srow0, int t, int end,
-                                         int lane, const uint32_t (&qa)[D / 16][4],
-                                         WarpState<D>& st) {
+__device__ __forceinline__ void load_sz(const DecodeParams& p, int64_t srow0, int start, int u0,
+                                        int cnt, int lane, uint32_t (&sz)[4]) {
+    const int r = lane >> 2, c = lane & 3;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int u = u0 + (e >> 1) * 8 + 2 * c + (e & 1);
+        if (u < cnt) {
+            const int64_t row = srow0 + start + u;
+            uint16_t sv, zv;
+            if constexpr (VG == 0) {
+                sv = __ldg(p.v_scale + row);
+                zv = __ldg(p.v_zero + row);
+            } else {
+                const int grp = (r * (D / 8)) / VG;
+                sv = __ldg(p.v_scale + row * (D / VG) + grp);
+                zv = __ldg(p.v_zero + row * (D / VG) + grp);
+            }
+            sz[e] = (uint32_t)sv | ((uint32_t)zv << 16);
+        } else {
+            sz[e] = 0u;
+        }
+    }
+}
+
+// ---- one 16-token tile of an fp8 / INT4 far stage ----
+template <int D, int VG>
+__device__ __forceinline__ void far_tile(const uint8_t* __restrict__ kbuf,
+                                         const uint8_t* __restrict__ vbuf, int u0, int cnt,
+                                         int gbase, int lane, const uint32_t (&qa)[D / 16][4],
+                                         const uint32_t (&sz)[4], WarpState<D>& st) {
     constexpr int KW = D / 16;    // u32 words of fp8 K per lane per token (D/4 bytes)
     constexpr int VB = D / 16;    // bytes of INT4 V per lane per token (D/8 dims)
     const int r = lane >> 2, c = lane & 3;
     uint32_t kr[2][KW];
 #pragma unroll
     for (int n = 0; n < 2; ++n) {
-        const int tok = t + 8 * n + r;
-        if (tok < end) {
-            const uint4* src =
-                reinterpret_cast<const uint4*>(p.far_k + (srow0 + tok) * D + c * (D / 4));
-#pragma unroll
-            for (int u = 0; u < KW / 4; ++u) {
-                const uint4 w = __ldg(src + u);
-                kr[n][4 * u] = w.x; kr[n][4 * u + 1] = w.y; kr[n][4 * u + 2] = w.z; kr[n][4 * u + 3] = w.w;
-            }
+        const int u = u0 + 8 * n + r;
+        const uint4* src = reinterpret_cast<const uint4*>(kbuf + u * D + c * (D / 4));
+        if constexpr (KW == 8) {
+            // odd rows read their second 16 bytes first: conflict-free phases
+            const int f = r & 1;
+            const uint4 w0 = src[f], w1 = src[f ^ 1];
+            const uint4 lo = f ? w1 : w0, hi = f ? w0 : w1;
+            kr[n][0] = lo.x; kr[n][1] = lo.y; kr[n][2] = lo.z; kr[n][3] = lo.w;
+            kr[n][4] = hi.x; kr[n][5] = hi.y; kr[n][6] = hi.z; kr[n][7] = hi.w;
         } else {
-#pragma unroll
-            for (int u = 0; u < KW; ++u) kr[n][u] = 0u;
+            const uint4 w = src[0];
+            kr[n][0] = w.x; kr[n][1] = w.y; kr[n][2] = w.z; kr[n][3] = w.w;
         }
     }
     uint32_t vr[4][(VB + 3) / 4];
-    uint16_t vs[4], vz[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-        const int tok = t + (e >> 1) * 8 + 2 * c + (e & 1);
-        if (tok < end) {
-            const int64_t row = srow0 + tok;
-            const uint8_t* src = p.far_v + row * (D / 2) + r * VB;
-            if constexpr (VB == 8) {
-                const uint2 w = __ldg(reinterpret_cast<const uint2*>(src));
-                vr[e][0] = w.x;
-                vr[e][1] = w.y;
-            } else {
-                vr[e][0] = __ldg(reinterpret_cast<const uint32_t*>(src));
-            }
-            if constexpr (VG == 0) {
-                vs[e] = __ldg(p.v_scale + row);
-                vz[e] = __ldg(p.v_zero + row);
-            } else {
-                const int grp = (r * (D / 8)) / VG;
-                vs[e] = __ldg(p.v_scale + row * (D / VG) + grp);
-                vz[e] = __ldg(p.v_zero + row * (D / VG) + grp);
-            }
+        const int u = u0 + (e >> 1) * 8 + 2 * c + (e & 1);
+        const bool ok = u < cnt;
+        const uint8_t* src = vbuf + u * (D / 2) + r * VB;
+        if constexpr (VB == 8) {
+            const uint2 w = ok ? *reinterpret_cast<const uint2*>(src) : make_uint2(0, 0);
+            vr[e][0] = w.x;
+            vr[e][1] = w.y;
         } else {
-#pragma unroll
-            for (int u = 0; u < (VB + 3) / 4; ++u) vr[e][u] = 0u;
-            vs[e] = 0;
-            vz[e] = 0;
+            vr[e][0] = ok ? *reinterpret_cast<const uint32_t*>(src) : 0u;
         }
     }
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
@@ -229,33 +273,62 @@ __device__ __forceinline__ void far_tile(const DecodeParams& p, int64_t srow0, i
     float s[4], pr[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-        const int tok = t + (j >> 1) * 8 + 2 * c + (j & 1);
+        const int u = u0 + (j >> 1) * 8 + 2 * c + (j & 1);
         const float v = sc[j >> 1][j & 1] + sc[j >> 1][2 + (j & 1)];
-        s[j] = tok < end ? v : -INFINITY;
-        if (tok < end && v > st.mf) {
+        s[j] = u < cnt ? v : -INFINITY;
+        if (u < cnt && v > st.mf) {
             st.mf = v;
-            st.af = tok;
+            st.af = gbase + u;
         }
     }
     st.softmax_step(s, pr, lane);
-    const uint32_t pb0 = pack_h2(pr[0], pr[1]);
-    const uint32_t pb1 = pack_h2(pr[2], pr[3]);
-    const uint32_t sAB = (uint32_t)vs[0] | ((uint32_t)vs[1] << 16);
-    const uint32_t zAB = (uint32_t)vz[0] | ((uint32_t)vz[1] << 16);
-    const uint32_t sCD = (uint32_t)vs[2] | ((uint32_t)vs[3] << 16);
-    const uint32_t zCD = (uint32_t)vz[2] | ((uint32_t)vz[3] << 16);
+    uint32_t pb0, pb1;
+    if constexpr (VG == 0) {
+        // per-token scale folded into P, zero into a running sum p * z:
+        // sum_t p_t (c_t s_t + z_t) = sum_t (p_t s_t) c_t + sum_t p_t z_t
+        float ps[4];
 #pragma unroll
-    for (int i = 0; i < D / 16; ++i) {
-        const int wi = i >> 2, bi = i & 3;
-        const uint32_t sel = (uint32_t)bi | ((uint32_t)(4 + bi) << 8);
-        const uint32_t xab = prmt(vr[0][wi], vr[1][wi], sel);
-        const uint32_t xcd = prmt(vr[2][wi], vr[3][wi], sel);
-        uint32_t a[4];
-        a[0] = dq_h2(nib2_to_h2(xab), sAB, zAB);
-        a[1] = dq_h2(nib2_to_h2(xab >> 4), sAB, zAB);
-        a[2] = dq_h2(nib2_to_h2(xcd), sCD, zCD);
-        a[3] = dq_h2(nib2_to_h2(xcd >> 4), sCD, zCD);
-        mma16816(st.o[i], a, pb0, pb1);
+        for (int e = 0; e < 4; ++e) {
+            const float sv = __half2float(__ushort_as_half(sz[e] & 0xFFFF));
+            const float zv = __half2float(__ushort_as_half(sz[e] >> 16));
+            ps[e] = pr[e] * sv;
+            st.z = fmaf(pr[e], zv, st.z);
+        }
+        pb0 = pack_h2(ps[0], ps[1]);
+        pb1 = pack_h2(ps[2], ps[3]);
+#pragma unroll
+        for (int i = 0; i < D / 16; ++i) {
+            const int wi = i >> 2, bi = i & 3;
+            const uint32_t sel = (uint32_t)bi | ((uint32_t)(4 + bi) << 8);
+            const uint32_t xab = prmt(vr[0][wi], vr[1][wi], sel);
+            const uint32_t xcd = prmt(vr[2][wi], vr[3][wi], sel);
+            uint32_t a[4];
+            a[0] = nib2_to_h2(xab);
+            a[1] = nib2_to_h2(xab >> 4);
+            a[2] = nib2_to_h2(xcd);
+            a[3] = nib2_to_h2(xcd >> 4);
+            mma16816(st.o[i], a, pb0, pb1);
+        }
+    } else {
+        pb0 = pack_h2(pr[0], pr[1]);
+        pb1 = pack_h2(pr[2], pr[3]);
+        const uint32_t sAB = (sz[0] & 0xFFFFu) | (sz[1] << 16);
+        const uint32_t zAB = (sz[0] >> 16) | (sz[1] & 0xFFFF0000u);
+        const uint32_t sCD = (sz[2] & 0xFFFFu) | (sz[3] << 16);
+        const uint32_t zCD = (sz[2] >> 16) | (sz[3] & 0xFFFF0000u);
+#pragma unroll
+        for (int i = 0; i < D / 16; ++i) {
+            const int wi = i >> 2, bi = i & 3;
+            const uint32_t sel = (uint32_t)bi | ((uint32_t)(4 + bi) << 8);
+            const uint32_t xab = prmt(vr[0][wi], vr[1][wi], sel);
+            const uint32_t xcd = prmt(vr[2][wi], vr[3][wi], sel);
+            uint32_t a[4];
+            a[0] = dq_h2(nib2_to_h2(xab), sAB, zAB);
+            a[1] = dq_h2(nib2_to_h2(xab >> 4), sAB, zAB);
+            a[2] = dq_h2(nib2_to_h2(xcd), sCD, zCD);
+            a[3] = dq_h2(nib2_to_h2(xcd >> 4), sCD, zCD);
+            mma16816(st.o[i], a, pb0, pb1);
+        }
     }
 }
 
@@ -268,7 +341,7 @@ __device__ __forceinline__ void merge_and_emit(const DecodeParams& p, const floa
     const int tid = threadIdx.x;
     const int b = s / p.Hk, h = s % p.Hk;
     auto ld = [&](const float* a) { return from_global ? __ldcg(a) : *a; };
-    for (int e = tid; e < kHeadsPerTile * D; e += kThreads) {
+    for (int e = tid; e < kHeadsPerTile * D; e += kConsumerThreads) {
         const int head = e / D, d = e % D;
         const int g = hg * kHeadsPerTile + head;
         if (g >= p.G) continue;
@@ -322,64 +395,139 @@ __device__ __forceinline__ void merge_and_emit(const DecodeParams& p, const floa
 }
 
 template <int D, int VG>
-__global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, 2) decode_fp8_kernel(const DecodeParams p) {
     using R = RecLayout<D>;
-    __shared__ float sh_rec[kWarps * R::SIZE];   // per-warp records, then CTA record
+    using RG = Ring<D>;
+    extern __shared__ __align__(128) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * RG::SLOT);
+    uint64_t* empty = full + kStages;
     __shared__ int sh_last;
     const int split = blockIdx.x, hg = blockIdx.y, s = blockIdx.z;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int r = lane >> 2, c = lane & 3;
 
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, kConsumerWarps);
+        }
+        fence_mbar_init();
+    }
+    // segments of this split's chunk [t0, t1) of [near valid | far | decode]
+    const int t0 = split * p.chunk;
+    const int t1 = min(t0 + p.chunk, p.Np + p.F + p.n_dec);
+    const int nv = min(max(__ldg(p.near_valid + s), 0), p.Np);
+    Segs sg;
+    sg.a[0] = t0;                       sg.e[0] = min(t1, nv);
+    sg.a[1] = max(t0, p.Np) - p.Np;     sg.e[1] = min(t1, p.Np + p.F) - p.Np;
+    sg.a[2] = max(t0, p.Np + p.F) - p.Np - p.F;
+    sg.e[2] = min(t1, p.Np + p.F + p.n_dec) - p.Np - p.F;
+    sg.n[0] = sg.e[0] > sg.a[0] ? (sg.e[0] - sg.a[0] + RG::NEAR_TOK - 1) / RG::NEAR_TOK : 0;
+    sg.n[1] = sg.e[1] > sg.a[1] ? (sg.e[1] - sg.a[1] + RG::FAR_TOK - 1) / RG::FAR_TOK : 0;
+    sg.n[2] = sg.e[2] > sg.a[2] ? (sg.e[2] - sg.a[2] + RG::NEAR_TOK - 1) / RG::NEAR_TOK : 0;
+    const int nstage = sg.n[0] + sg.n[1] + sg.n[2];
+    __syncthreads();
+
+    if (w == kConsumerWarps) {
+        // ---------------- producer warp: one elected lane issues bulk copies
+        if (lane == 0) {
+            const uint8_t* nk = reinterpret_cast<const uint8_t*>(p.near_k) + (int64_t)s * p.Np * D * 2;
+            const uint8_t* nvp = reinterpret_cast<const uint8_t*>(p.near_v) + (int64_t)s * p.Np * D * 2;
+            const uint8_t* fk = p.far_k + (int64_t)s * p.F * D;
+            const uint8_t* fv = p.far_v + (int64_t)s * p.F * (D / 2);
+            const uint8_t* dk = reinterpret_cast<const uint8_t*>(p.dec_k) + (int64_t)s * p.dec_stride * D * 2;
+            const uint8_t* dv = reinterpret_cast<const uint8_t*>(p.dec_v) + (int64_t)s * p.dec_stride * D * 2;
+            for (int k = 0; k < nstage; ++k) {
+                const int slot = k % kStages;
+                if (k >= kStages && !mbar_wait(empty + slot, ((k / kStages) - 1) & 1)) {
+                    atomicExch(p.status, FKV_ERR_TIMEOUT);
+                    break;
+                }
+                int seg, start, cnt;
+                stage_at<D>(sg, k, seg, start, cnt);
+                uint8_t* dst = smem + slot * RG::SLOT;
+                const uint8_t *ks, *vs;
+                uint32_t kb, vb;
+                if (seg == 1) {
+                    ks = fk + (int64_t)start * D;
+                    vs = fv + (int64_t)start * (D / 2);
+                    kb = cnt * D;
+                    vb = cnt * (D / 2);
+                } else {
+                    ks = (seg == 0 ? nk : dk) + (int64_t)start * D * 2;
+                    vs = (seg == 0 ? nvp : dv) + (int64_t)start * D * 2;
+                    kb = vb = cnt * D * 2;
+                }
+                mbar_arrive_expect_tx(full + slot, kb + vb);
+                bulk_g2s(dst, ks, kb, full + slot);
+                bulk_g2s(dst + RG::VOFF, vs, vb, full + slot);
+            }
+        }
+        return;
+    }
+
+    // ---------------- consumer warps
     uint32_t qa[D / 16][4];
     build_q_frags<D>(p, s, hg, lane, qa);
     WarpState<D> st;
     st.init();
+    const int64_t srow0 = (int64_t)s * p.F;
+    uint32_t szc[2][4], szn[2][4];
+    auto prefetch = [&](int k, uint32_t (&dst)[2][4]) {
+        if (k >= nstage) return;
+        int seg, start, cnt;
+        stage_at<D>(sg, k, seg, start, cnt);
+        if (seg != 1) return;
+#pragma unroll
+        for (int x = 0; x < 2; ++x) load_sz<D, VG>(p, srow0, start, (w + 4 * x) * kTile, cnt, lane, dst[x]);
+    };
+    prefetch(0, szc);
+    int failed_at = -1;
+    for (int k = 0; k < nstage; ++k) {
+        const int slot = k % kStages;
+        int seg, start, cnt;
+        stage_at<D>(sg, k, seg, start, cnt);
+        prefetch(k + 1, szn);
+        if (!mbar_wait(full + slot, (k / kStages) & 1)) {
+            atomicExch(p.status, FKV_ERR_TIMEOUT);
+            failed_at = k;
+            break;
+        }
+        const uint8_t* kbuf = smem + slot * RG::SLOT;
+        const uint8_t* vbuf = kbuf + RG::VOFF;
+        const int ntile = (cnt + kTile - 1) / kTile;
+        if (seg == 1) {
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+                const int i = w + 4 * x;
+                if (i < ntile) far_tile<D, VG>(kbuf, vbuf, i * kTile, cnt, start, lane, qa, szc[x], st);
+            }
+        } else if (w < ntile) {
+            fp16_tile<D>(kbuf, vbuf, w * kTile, cnt, lane, qa, st);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + slot);
+#pragma unroll
+        for (int x = 0; x < 2; ++x)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) szc[x][e] = szn[x][e];
+    }
+    if (failed_at >= 0) {
+        // the producer runs at most kStages ahead of the consumers: wait
+        // (bounded) for the copies it may still have in flight, then leave
+        for (int k = failed_at; k < min(nstage, failed_at + kStages); ++k)
+            if (!mbar_wait(full + (k % kStages), (k / kStages) & 1)) break;
+    }
 
-    const int t0 = split * p.chunk;
-    const int t1 = min(t0 + p.chunk, p.Np + p.F + p.n_dec);
-    const int nv = min(max(__ldg(p.near_valid + s), 0), p.Np);
-    int tile_base = 0;
-    // near tier [0, nv)
-    {
-        const int a = max(t0, 0), e = min(t1, nv);
-        if (a < e) {
-            const uint16_t* kb = p.near_k + (int64_t)s * p.Np * D;
-            const uint16_t* vb = p.near_v + (int64_t)s * p.Np * D;
-            const int nt = (e - a + kTile - 1) / kTile;
-            for (int i = (w - tile_base % kWarps + kWarps) % kWarps; i < nt; i += kWarps)
-                fp16_tile<D>(kb, vb, a + i * kTile, e, lane, qa, st);
-            tile_base += nt;
-        }
-    }
-    // far tier [Np, Np+F)
-    {
-        const int a = max(t0, p.Np) - p.Np, e = min(t1, p.Np + p.F) - p.Np;
-        if (a < e) {
-            const int nt = (e - a + kTile - 1) / kTile;
-            const int64_t srow0 = (int64_t)s * p.F;
-            for (int i = (w - tile_base % kWarps + kWarps) % kWarps; i < nt; i += kWarps)
-                far_tile<D, VG>(p, srow0, a + i * kTile, e, lane, qa, st);
-            tile_base += nt;
-        }
-    }
-    // decode buffer [Np+F, Np+F+n_dec)
-    {
-        const int base = p.Np + p.F;
-        const int a = max(t0, base) - base, e = min(t1, base + p.n_dec) - base;
-        if (a < e) {
-            const uint16_t* kb = p.dec_k + (int64_t)s * p.dec_stride * D;
-            const uint16_t* vb = p.dec_v + (int64_t)s * p.dec_stride * D;
-            const int nt = (e - a + kTile - 1) / kTile;
-            for (int i = (w - tile_base % kWarps + kWarps) % kWarps; i < nt; i += kWarps)
-                fp16_tile<D>(kb, vb, a + i * kTile, e, lane, qa, st);
-            tile_base += nt;
-        }
-    }
-
-    // ---- warp record -> shared memory
+    // ---- warp record -> shared memory (the ring is free once all consumers pass)
+    const int r = lane >> 2, c = lane & 3;
     st.l = quad_sum(st.l);
+    st.z = quad_sum(st.z);
     st.mn = quad_min(st.mn);
     quad_argmax(st.mf, st.af);
+    const float z0 = __shfl_sync(0xffffffffu, st.z, (2 * c) * 4);
+    const float z1 = __shfl_sync(0xffffffffu, st.z, (2 * c + 1) * 4);
+    named_sync(1, kConsumerThreads);
+    float* sh_rec = reinterpret_cast<float*>(smem);
     float* wr = sh_rec + w * R::SIZE;
     if (c == 0) {
         wr[R::M + r] = st.m;
@@ -391,31 +539,31 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
 #pragma unroll
     for (int i = 0; i < D / 16; ++i) {
         const int d0 = r * (D / 8) + 2 * i;
-        wr[R::O + (2 * c) * D + d0] = st.o[i][0];
-        wr[R::O + (2 * c + 1) * D + d0] = st.o[i][1];
-        wr[R::O + (2 * c) * D + d0 + 1] = st.o[i][2];
-        wr[R::O + (2 * c + 1) * D + d0 + 1] = st.o[i][3];
+        wr[R::O + (2 * c) * D + d0] = st.o[i][0] + z0;
+        wr[R::O + (2 * c + 1) * D + d0] = st.o[i][1] + z1;
+        wr[R::O + (2 * c) * D + d0 + 1] = st.o[i][2] + z0;
+        wr[R::O + (2 * c + 1) * D + d0 + 1] = st.o[i][3] + z1;
     }
-    __syncthreads();
+    named_sync(1, kConsumerThreads);
 
     if (p.splits == 1) {
-        merge_and_emit<D>(p, sh_rec, kWarps, R::SIZE, s, hg, false);
+        merge_and_emit<D>(p, sh_rec, kConsumerWarps, R::SIZE, s, hg, false);
         return;
     }
 
     // ---- CTA record -> workspace, then the last CTA of this stream merges
-    const int64_t slot = ((int64_t)s * p.HG + hg) * p.splits + split;
-    float* gr = p.ws + slot * R::SIZE;
-    for (int e = threadIdx.x; e < 8 * D + 8; e += kThreads) {
+    const int64_t slotrec = ((int64_t)s * p.HG + hg) * p.splits + split;
+    float* gr = p.ws + slotrec * R::SIZE;
+    for (int e = threadIdx.x; e < 8 * D + 8; e += kConsumerThreads) {
         if (e < 8 * D) {
             const int head = e / D;
             float M = -INFINITY;
 #pragma unroll
-            for (int k = 0; k < kWarps; ++k) M = fmaxf(M, sh_rec[k * R::SIZE + R::M + head]);
+            for (int k = 0; k < kConsumerWarps; ++k) M = fmaxf(M, sh_rec[k * R::SIZE + R::M + head]);
             float acc = 0.f;
             if (M != -INFINITY) {
 #pragma unroll
-                for (int k = 0; k < kWarps; ++k) {
+                for (int k = 0; k < kConsumerWarps; ++k) {
                     const float mk = sh_rec[k * R::SIZE + R::M + head];
                     if (mk != -INFINITY)
                         acc = fmaf(exp2f((mk - M) * kLog2e), sh_rec[k * R::SIZE + R::O + e], acc);
@@ -427,9 +575,9 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
             float M = -INFINITY, L = 0.f, mn = INFINITY, mf = -INFINITY;
             int af = -1;
 #pragma unroll
-            for (int k = 0; k < kWarps; ++k) M = fmaxf(M, sh_rec[k * R::SIZE + R::M + head]);
+            for (int k = 0; k < kConsumerWarps; ++k) M = fmaxf(M, sh_rec[k * R::SIZE + R::M + head]);
 #pragma unroll
-            for (int k = 0; k < kWarps; ++k) {
+            for (int k = 0; k < kConsumerWarps; ++k) {
                 const float* q = sh_rec + k * R::SIZE;
                 if (q[R::M + head] != -INFINITY)
                     L = fmaf(exp2f((q[R::M + head] - M) * kLog2e), q[R::L + head], L);
@@ -444,14 +592,14 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
         }
     }
     __threadfence();
-    __syncthreads();
+    named_sync(1, kConsumerThreads);
     if (threadIdx.x == 0) {
         int* tk = p.tickets + ((int64_t)s * p.HG + hg);
         const int old = atomicAdd(tk, 1);
         sh_last = (old == p.splits - 1);
         if (sh_last) *tk = 0;   // every other CTA of this stream has arrived
     }
-    __syncthreads();
+    named_sync(1, kConsumerThreads);
     if (!sh_last) return;
     __threadfence();
     const float* base = p.ws + ((int64_t)s * p.HG + hg) * p.splits * R::SIZE;
@@ -521,19 +669,20 @@ Plan make_plan(const FkvDecodeShape* sh) {
     const int64_t streams = (int64_t)sh->B * sh->Hk * pl.HG;
     int splits = sh->num_splits;
     if (splits <= 0) {
-        // aim for >= 8 waves of 3 resident CTAs per SM, chunks of >= 512 tokens
-        const int64_t target = (int64_t)num_sms() * 3 * 8;
+        // aim for >= 8 waves of 2 resident CTAs per SM, chunks of >= 512 tokens
+        const int64_t target = (int64_t)num_sms() * 2 * 8;
         int64_t want = (target + streams - 1) / streams;
         const int64_t max_by_len = std::max<int64_t>(1, (T + 511) / 512);
         splits = (int)std::max<int64_t>(1, std::min(want, max_by_len));
     }
     int64_t chunk = (T + splits - 1) / splits;
-    chunk = std::max<int64_t>(kTile * kWarps, (chunk + kTile * kWarps - 1) / (kTile * kWarps) * (kTile * kWarps));
+    constexpr int64_t q = 64;   // chunk granularity (tokens)
+    chunk = std::max<int64_t>(q, (chunk + q - 1) / q * q);
     pl.splits = (int)std::max<int64_t>(1, (T + chunk - 1) / chunk);
     pl.chunk = (int)chunk;
     const int D = sh->D;
     pl.rec_bytes = pl.splits > 1 ? (size_t)streams * pl.splits * (40 + 8 * D) * sizeof(float) : 0;
-    pl.ticket_bytes = (size_t)streams * sizeof(int32_t);
+    pl.ticket_bytes = 16 + (size_t)streams * sizeof(int32_t);   // status word + counters
     return pl;
 }
 
@@ -556,6 +705,23 @@ int validate(const FkvDecodeShape* sh) {
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
+// Opt every kernel instantiation into its dynamic shared memory once per
+// device, then launch.
+int launch_kernel(void (*kern)(DecodeParams), int smem, dim3 grid, const DecodeParams& p,
+                  cudaStream_t st) {
+    static thread_local std::vector<std::pair<int, const void*>> done;
+    int dev = 0;
+    FKV_CUDA_CHECK(cudaGetDevice(&dev));
+    const std::pair<int, const void*> key{dev, (const void*)kern};
+    if (std::find(done.begin(), done.end(), key) == done.end()) {
+        FKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        done.push_back(key);
+    }
+    kern<<<grid, kThreads, smem, st>>>(p);
+    FKV_LAUNCH_CHECK();
+    return FKV_OK;
+}
+
 int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws_bytes,
            cudaStream_t st) {
     const Plan pl = make_plan(sh);
@@ -570,21 +736,19 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     // split counters at the front, split records at the back: a workspace
     // shared by calls of different shapes keeps every counter at zero as long
     // as it holds the largest records region plus the largest counter region.
-    p.tickets = reinterpret_cast<int32_t*>(workspace);
+    p.status = reinterpret_cast<int32_t*>(workspace);
+    p.tickets = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(workspace) + 16);
     const size_t rec_off = (ws_bytes - pl.rec_bytes) & ~(size_t)255;
     FKV_REQUIRE(rec_off >= pl.ticket_bytes, FKV_ERR_INVALID,
                 "workspace too small for counters + records (%zu bytes)", ws_bytes);
     p.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + rec_off);
     dim3 grid(pl.splits, pl.HG, sh->B * sh->Hk);
     if (sh->D == 128) {
-        if (sh->v_group == 0) decode_fp8_kernel<128, 0><<<grid, kThreads, 0, st>>>(p);
-        else decode_fp8_kernel<128, 32><<<grid, kThreads, 0, st>>>(p);
-    } else {
-        if (sh->v_group == 0) decode_fp8_kernel<64, 0><<<grid, kThreads, 0, st>>>(p);
-        else decode_fp8_kernel<64, 32><<<grid, kThreads, 0, st>>>(p);
+        if (sh->v_group == 0) return launch_kernel(decode_fp8_kernel<128, 0>, Ring<128>::BYTES, grid, p, st);
+        return launch_kernel(decode_fp8_kernel<128, 32>, Ring<128>::BYTES, grid, p, st);
     }
-    FKV_LAUNCH_CHECK();
-    return FKV_OK;
+    if (sh->v_group == 0) return launch_kernel(decode_fp8_kernel<64, 0>, Ring<64>::BYTES, grid, p, st);
+    return launch_kernel(decode_fp8_kernel<64, 32>, Ring<64>::BYTES, grid, p, st);
 }
 
 int fill_common(const FkvDecodeShape* sh, DecodeParams& p, const uint16_t* near_k,
@@ -601,7 +765,7 @@ int fill_common(const FkvDecodeShape* sh, DecodeParams& p, const uint16_t* near_
                 "far tier pointer is NULL");
     FKV_REQUIRE(sh->n_dec == 0 || (dec_k && dec_v), FKV_ERR_INVALID, "decode buffer is NULL");
     FKV_REQUIRE(aligned16(q) && aligned16(near_k) && aligned16(near_v) && aligned16(far_k) &&
-                    aligned16(dec_k) && aligned16(dec_v) && ((uintptr_t)far_v & 3u) == 0 &&
+                    aligned16(dec_k) && aligned16(dec_v) && aligned16(far_v) &&
                     ((uintptr_t)v_scale & 1u) == 0 && ((uintptr_t)v_zero & 1u) == 0,
                 FKV_ERR_INVALID, "tier / query pointers misaligned");
     p = DecodeParams{};
