@@ -45,6 +45,14 @@ __device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t two_bytes) {
     return (uint32_t)h.x | ((uint32_t)h.y << 16);
 }
 
+// four E4M3 codes of one word -> (bytes 0,1) and (bytes 2,3) as f16x2 pairs
+__device__ __forceinline__ void e4m3x4_to_h2x2(uint32_t w, uint32_t& lo, uint32_t& hi) {
+    asm("{\n .reg .b16 a, b;\n mov.b32 {a, b}, %2;\n"
+        " cvt.rn.f16x2.e4m3x2 %0, a;\n cvt.rn.f16x2.e4m3x2 %1, b;\n}\n"
+        : "=r"(lo), "=r"(hi)
+        : "r"(w));
+}
+
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return __byte_perm(a, b, sel);
 }
@@ -121,10 +129,14 @@ struct WarpState {
         af = -1;
     }
 
-    // online-softmax update with the tile's 4 scores (masked = -inf);
-    // returns the unnormalised probabilities in p[].
-    __device__ __forceinline__ void softmax_step(const float (&s)[4], float (&p)[4], int lane) {
-        const float tmax = quad_max(fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3])));
+    // online-softmax update with this lane's N scores of head r (masked =
+    // -inf); returns the unnormalised probabilities in p[].
+    template <int N>
+    __device__ __forceinline__ void softmax_step(const float (&s)[N], float (&p)[N], int lane) {
+        float lm = s[0];
+#pragma unroll
+        for (int j = 1; j < N; ++j) lm = fmaxf(lm, s[j]);
+        const float tmax = quad_max(lm);
         const bool up = tmax > m;
         if (__any_sync(0xffffffffu, up)) {
             const float mnew = up ? tmax : m;
@@ -145,7 +157,7 @@ struct WarpState {
         }
         const float mb = m * kLog2e;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < N; ++j) {
             p[j] = exp2f(fmaf(s[j], kLog2e, -mb));   // s = -inf -> 0
             l += p[j];
         }

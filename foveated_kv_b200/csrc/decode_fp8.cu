@@ -224,110 +224,134 @@ __device__ __forceinline__ void load_sz(const DecodeParams& p, int64_t srow0, in
     }
 }
 
-// ---- one 16-token tile of an fp8 / INT4 far stage ----
-template <int D, int VG>
-__device__ __forceinline__ void far_tile(const uint8_t* __restrict__ kbuf,
-                                         const uint8_t* __restrict__ vbuf, int u0, int cnt,
-                                         int gbase, int lane, const uint32_t (&qa)[D / 16][4],
-                                         const uint32_t (&sz)[4], WarpState<D>& st) {
+// ---- NT 16-token tiles of an fp8 / INT4 far stage, processed jointly ----
+// (the tiles' loads, conversions and tensor-core products are interleaved and
+// share one online-softmax step, which gives each warp instruction-level
+// parallelism at the occupancy the register budget allows)
+template <int D, int VG, int NT>
+__device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
+                                          const uint8_t* __restrict__ vbuf, const int (&u0)[NT],
+                                          int cnt, int gbase, int lane,
+                                          const uint32_t (&qa)[D / 16][4],
+                                          const uint32_t (&sz)[NT][4], WarpState<D>& st) {
     constexpr int KW = D / 16;    // u32 words of fp8 K per lane per token (D/4 bytes)
     constexpr int VB = D / 16;    // bytes of INT4 V per lane per token (D/8 dims)
+    constexpr int VWN = (VB + 3) / 4;
     const int r = lane >> 2, c = lane & 3;
-    uint32_t kr[2][KW];
+    uint32_t kr[NT][2][KW];
+    uint32_t vr[NT][4][VWN];
 #pragma unroll
-    for (int n = 0; n < 2; ++n) {
-        const int u = u0 + 8 * n + r;
-        const uint4* src = reinterpret_cast<const uint4*>(kbuf + u * D + c * (D / 4));
-        if constexpr (KW == 8) {
-            // odd rows read their second 16 bytes first: conflict-free phases
-            const int f = r & 1;
-            const uint4 w0 = src[f], w1 = src[f ^ 1];
-            const uint4 lo = f ? w1 : w0, hi = f ? w0 : w1;
-            kr[n][0] = lo.x; kr[n][1] = lo.y; kr[n][2] = lo.z; kr[n][3] = lo.w;
-            kr[n][4] = hi.x; kr[n][5] = hi.y; kr[n][6] = hi.z; kr[n][7] = hi.w;
-        } else {
-            const uint4 w = src[0];
-            kr[n][0] = w.x; kr[n][1] = w.y; kr[n][2] = w.z; kr[n][3] = w.w;
+    for (int t = 0; t < NT; ++t) {
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+            const int u = u0[t] + 8 * n + r;
+            const uint4* src = reinterpret_cast<const uint4*>(kbuf + u * D + c * (D / 4));
+            if constexpr (KW == 8) {
+                // odd rows read their second 16 bytes first: conflict-free phases
+                const int f = r & 1;
+                const uint4 w0 = src[f], w1 = src[f ^ 1];
+                const uint4 lo = f ? w1 : w0, hi = f ? w0 : w1;
+                kr[t][n][0] = lo.x; kr[t][n][1] = lo.y; kr[t][n][2] = lo.z; kr[t][n][3] = lo.w;
+                kr[t][n][4] = hi.x; kr[t][n][5] = hi.y; kr[t][n][6] = hi.z; kr[t][n][7] = hi.w;
+            } else {
+                const uint4 w = src[0];
+                kr[t][n][0] = w.x; kr[t][n][1] = w.y; kr[t][n][2] = w.z; kr[t][n][3] = w.w;
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int u = u0[t] + (e >> 1) * 8 + 2 * c + (e & 1);
+            const bool ok = u < cnt;
+            const uint8_t* src = vbuf + u * (D / 2) + r * VB;
+            if constexpr (VB == 8) {
+                const uint2 w = ok ? *reinterpret_cast<const uint2*>(src) : make_uint2(0, 0);
+                vr[t][e][0] = w.x;
+                vr[t][e][1] = w.y;
+            } else {
+                vr[t][e][0] = ok ? *reinterpret_cast<const uint32_t*>(src) : 0u;
+            }
         }
     }
-    uint32_t vr[4][(VB + 3) / 4];
+    float sc[NT][2][4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        const int u = u0 + (e >> 1) * 8 + 2 * c + (e & 1);
-        const bool ok = u < cnt;
-        const uint8_t* src = vbuf + u * (D / 2) + r * VB;
-        if constexpr (VB == 8) {
-            const uint2 w = ok ? *reinterpret_cast<const uint2*>(src) : make_uint2(0, 0);
-            vr[e][0] = w.x;
-            vr[e][1] = w.y;
-        } else {
-            vr[e][0] = ok ? *reinterpret_cast<const uint32_t*>(src) : 0u;
-        }
-    }
-    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int n = 0; n < 2; ++n) sc[t][n][0] = sc[t][n][1] = sc[t][n][2] = sc[t][n][3] = 0.f;
 #pragma unroll
     for (int j = 0; j < D / 16; ++j) {
-        mma16816(sc[0], qa[j], e4m3x2_to_h2(kr[0][j]), e4m3x2_to_h2(kr[0][j] >> 16));
-        mma16816(sc[1], qa[j], e4m3x2_to_h2(kr[1][j]), e4m3x2_to_h2(kr[1][j] >> 16));
-    }
-    float s[4], pr[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const int u = u0 + (j >> 1) * 8 + 2 * c + (j & 1);
-        const float v = sc[j >> 1][j & 1] + sc[j >> 1][2 + (j & 1)];
-        s[j] = u < cnt ? v : -INFINITY;
-        if (u < cnt && v > st.mf) {
-            st.mf = v;
-            st.af = gbase + u;
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int n = 0; n < 2; ++n) {
+                uint32_t b0, b1;
+                e4m3x4_to_h2x2(kr[t][n][j], b0, b1);
+                mma16816(sc[t][n], qa[j], b0, b1);
+            }
+        }
+    }
+    float s[4 * NT], pr[4 * NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int u = u0[t] + (j >> 1) * 8 + 2 * c + (j & 1);
+            const float v = sc[t][j >> 1][j & 1] + sc[t][j >> 1][2 + (j & 1)];
+            s[4 * t + j] = u < cnt ? v : -INFINITY;
+            if (u < cnt && v > st.mf) {   // lane's tokens arrive in increasing order
+                st.mf = v;
+                st.af = gbase + u;
+            }
         }
     }
     st.softmax_step(s, pr, lane);
-    uint32_t pb0, pb1;
-    if constexpr (VG == 0) {
-        // per-token scale folded into P, zero into a running sum p * z:
-        // sum_t p_t (c_t s_t + z_t) = sum_t (p_t s_t) c_t + sum_t p_t z_t
-        float ps[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float sv = __half2float(__ushort_as_half(sz[e] & 0xFFFF));
-            const float zv = __half2float(__ushort_as_half(sz[e] >> 16));
-            ps[e] = pr[e] * sv;
-            st.z = fmaf(pr[e], zv, st.z);
-        }
-        pb0 = pack_h2(ps[0], ps[1]);
-        pb1 = pack_h2(ps[2], ps[3]);
+    for (int t = 0; t < NT; ++t) {
+        uint32_t pb0, pb1;
+        if constexpr (VG == 0) {
+            // per-token scale folded into P, zero into a running sum p * z:
+            // sum_t p_t (c_t s_t + z_t) = sum_t (p_t s_t) c_t + sum_t p_t z_t
+            float ps[4];
 #pragma unroll
-        for (int i = 0; i < D / 16; ++i) {
-            const int wi = i >> 2, bi = i & 3;
-            const uint32_t sel = (uint32_t)bi | ((uint32_t)(4 + bi) << 8);
-            const uint32_t xab = prmt(vr[0][wi], vr[1][wi], sel);
-            const uint32_t xcd = prmt(vr[2][wi], vr[3][wi], sel);
-            uint32_t a[4];
-            a[0] = nib2_to_h2(xab);
-            a[1] = nib2_to_h2(xab >> 4);
-            a[2] = nib2_to_h2(xcd);
-            a[3] = nib2_to_h2(xcd >> 4);
-            mma16816(st.o[i], a, pb0, pb1);
-        }
-    } else {
-        pb0 = pack_h2(pr[0], pr[1]);
-        pb1 = pack_h2(pr[2], pr[3]);
-        const uint32_t sAB = (sz[0] & 0xFFFFu) | (sz[1] << 16);
-        const uint32_t zAB = (sz[0] >> 16) | (sz[1] & 0xFFFF0000u);
-        const uint32_t sCD = (sz[2] & 0xFFFFu) | (sz[3] << 16);
-        const uint32_t zCD = (sz[2] >> 16) | (sz[3] & 0xFFFF0000u);
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __half22float2(u32_as_h2(sz[t][e]));   // (scale, zero)
+                ps[e] = pr[4 * t + e] * f.x;
+                st.z = fmaf(pr[4 * t + e], f.y, st.z);
+            }
+            pb0 = pack_h2(ps[0], ps[1]);
+            pb1 = pack_h2(ps[2], ps[3]);
 #pragma unroll
-        for (int i = 0; i < D / 16; ++i) {
-            const int wi = i >> 2, bi = i & 3;
-            const uint32_t sel = (uint32_t)bi | ((uint32_t)(4 + bi) << 8);
-            const uint32_t xab = prmt(vr[0][wi], vr[1][wi], sel);
-            const uint32_t xcd = prmt(vr[2][wi], vr[3][wi], sel);
-            uint32_t a[4];
-            a[0] = dq_h2(nib2_to_h2(xab), sAB, zAB);
-            a[1] = dq_h2(nib2_to_h2(xab >> 4), sAB, zAB);
-            a[2] = dq_h2(nib2_to_h2(xcd), sCD, zCD);
-            a[3] = dq_h2(nib2_to_h2(xcd >> 4), sCD, zCD);
-            mma16816(st.o[i], a, pb0, pb1);
+            for (int i = 0; i < D / 16; ++i) {
+                const int wi = i >> 2, bi = i & 3;
+                const uint32_t sel = (uint32_t)bi | ((uint32_t)(4 + bi) << 8);
+                const uint32_t xab = prmt(vr[t][0][wi], vr[t][1][wi], sel);
+                const uint32_t xcd = prmt(vr[t][2][wi], vr[t][3][wi], sel);
+                uint32_t a[4];
+                a[0] = nib2_to_h2(xab);
+                a[1] = nib2_to_h2(xab >> 4);
+                a[2] = nib2_to_h2(xcd);
+                a[3] = nib2_to_h2(xcd >> 4);
+                mma16816(st.o[i], a, pb0, pb1);
+            }
+        } else {
+            pb0 = pack_h2(pr[4 * t + 0], pr[4 * t + 1]);
+            pb1 = pack_h2(pr[4 * t + 2], pr[4 * t + 3]);
+            const uint32_t sAB = (sz[t][0] & 0xFFFFu) | (sz[t][1] << 16);
+            const uint32_t zAB = (sz[t][0] >> 16) | (sz[t][1] & 0xFFFF0000u);
+            const uint32_t sCD = (sz[t][2] & 0xFFFFu) | (sz[t][3] << 16);
+            const uint32_t zCD = (sz[t][2] >> 16) | (sz[t][3] & 0xFFFF0000u);
+#pragma unroll
+            for (int i = 0; i < D / 16; ++i) {
+                const int wi = i >> 2, bi = i & 3;
+                const uint32_t sel = (uint32_t)bi | ((uint32_t)(4 + bi) << 8);
+                const uint32_t xab = prmt(vr[t][0][wi], vr[t][1][wi], sel);
+                const uint32_t xcd = prmt(vr[t][2][wi], vr[t][3][wi], sel);
+                uint32_t a[4];
+                a[0] = dq_h2(nib2_to_h2(xab), sAB, zAB);
+                a[1] = dq_h2(nib2_to_h2(xab >> 4), sAB, zAB);
+                a[2] = dq_h2(nib2_to_h2(xcd), sCD, zCD);
+                a[3] = dq_h2(nib2_to_h2(xcd >> 4), sCD, zCD);
+                mma16816(st.o[i], a, pb0, pb1);
+            }
         }
     }
 }
@@ -496,10 +520,13 @@ __global__ void __launch_bounds__(kThreads, 2) decode_fp8_kernel(const DecodePar
         const uint8_t* vbuf = kbuf + RG::VOFF;
         const int ntile = (cnt + kTile - 1) / kTile;
         if (seg == 1) {
-#pragma unroll
-            for (int x = 0; x < 2; ++x) {
-                const int i = w + 4 * x;
-                if (i < ntile) far_tile<D, VG>(kbuf, vbuf, i * kTile, cnt, start, lane, qa, szc[x], st);
+            if (w + 4 < ntile) {
+                const int u0[2] = {w * kTile, (w + 4) * kTile};
+                far_tiles<D, VG, 2>(kbuf, vbuf, u0, cnt, start, lane, qa, szc, st);
+            } else if (w < ntile) {
+                const int u0[1] = {w * kTile};
+                const uint32_t (&sz1)[1][4] = *reinterpret_cast<const uint32_t (*)[1][4]>(&szc[0]);
+                far_tiles<D, VG, 1>(kbuf, vbuf, u0, cnt, start, lane, qa, sz1, st);
             }
         } else if (w < ntile) {
             fp16_tile<D>(kbuf, vbuf, w * kTile, cnt, lane, qa, st);
