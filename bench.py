@@ -9,8 +9,10 @@ fp16 K/V/q with 4 outlier K channels per head (there is no dataset for this
 path).  Weak scaling: each rank holds its own 64 sequences; no collective on
 the data path.
 
-One step = one fused decode launch of the layer (all 64 sequences).  Metric:
-decode tokens/s = sequences / (32 layers x per-layer time), attention only.
+One step = one fused decode launch per layer for L distinct layers (L = 32,
+or fewer when 32 layers would exceed ~4 GB of tiers), captured once in a CUDA
+graph and replayed; per-layer time = step time / L.  Metric: decode tokens/s
+= sequences / (32 layers x per-layer time), attention only.
 ``value`` uses device-resident inputs; ``e2e`` goes through the public API
 (FoveatedLayer.attend_fused_with_spikes) with the query copied from pinned
 host memory and output + spike flags/tokens read back every step.
@@ -219,26 +221,45 @@ def main():
 
     c, cfg, lay, q = build_layer(args.config, 1000 + rank, device, args.batch)
     B, Hq, Hk, D = c["B"], c["Hq"], c["Hk"], c["D"]
-    st = torch.cuda.current_stream()
-    out = torch.empty((B, Hq, 1, D), dtype=torch.float16, device=device)
+    tier_bytes = sum(t.numel() * t.element_size() for t in (
+        lay.near_k, lay.near_v, lay.far_k, lay.far_v, lay.far_v_scale, lay.far_v_zero))
+    # distinct layers so that one graph replay streams >= ~4 GB (no L2 reuse
+    # across layers); c0 fits in L2 whatever we do and is reported as latency
+    n_layers = max(1, min(N_LAYERS, int(4e9 // max(tier_bytes, 1))))
+    layers = [lay] + [build_layer(args.config, 2000 + 97 * i + rank, device, args.batch)[2]
+                      for i in range(1, n_layers)]
+    for L_ in layers[1:]:
+        L_.archive_k = L_.archive_v = None
+    st = torch.cuda.Stream(device)
+    outs = [torch.empty((B, Hq, 1, D), dtype=torch.float16, device=device) for _ in layers]
 
     def step():
-        return lay.attend_fused_with_spikes(q, out=out)
+        for L_, o in zip(layers, outs):
+            L_.attend_fused_with_spikes(q, out=o)
 
-    for _ in range(max(args.warmup, 3)):
+    with torch.cuda.stream(st):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=st):
         step()
+    torch.cuda.synchronize()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
     with ClockSampler(local) as clk:
-        e0.record(st)
+        e0.record(cur)
         for _ in range(args.steps):
-            step()
-        e1.record(st)
+            graph.replay()
+        e1.record(cur)
         torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    ms = e0.elapsed_time(e1) / (args.steps * n_layers)      # per layer
     if world > 1:
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -247,6 +268,7 @@ def main():
     alg = algorithmic_bytes(B, Hq, Hk, D, nv_sum, lay.n_far, lay.n_decode,
                             cfg.compress_method == "turbo")
     value = world * B / (N_LAYERS * ms * 1e-3)
+    st = cur
 
     # ---- e2e through the public API: pinned H2D of q, D2H of out+flags+tokens
     q_host = q.cpu().pin_memory()
@@ -309,7 +331,8 @@ def main():
                          "algorithmic_bytes_per_launch": alg, "traffic": None},
             "e2e": {"value": world * B / (N_LAYERS * ms_e2e * 1e-3), "unit": "tokens/s",
                     "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * n_layers,
+            "layers_per_graph": n_layers,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }

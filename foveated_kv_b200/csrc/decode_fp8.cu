@@ -696,11 +696,24 @@ Plan make_plan(const FkvDecodeShape* sh) {
     const int64_t streams = (int64_t)sh->B * sh->Hk * pl.HG;
     int splits = sh->num_splits;
     if (splits <= 0) {
-        // aim for >= 8 waves of 2 resident CTAs per SM, chunks of >= 512 tokens
-        const int64_t target = (int64_t)num_sms() * 2 * 8;
-        int64_t want = (target + streams - 1) / streams;
-        const int64_t max_by_len = std::max<int64_t>(1, (T + 511) / 512);
-        splits = (int)std::max<int64_t>(1, std::min(want, max_by_len));
+        // Pick the split count minimising (waves of resident CTAs) x (chunk
+        // length + a fixed per-CTA cost of ~384 tokens: pipeline fill, record
+        // write and merge).  Balances wave quantisation against CTA overhead:
+        // few long CTAs for a handful of (b, kv head) streams, a few splits
+        // for large batches.
+        const int64_t slots = (int64_t)num_sms() * 2;
+        double best = 1e300;
+        splits = 1;
+        for (int sp = 1; sp <= 64; ++sp) {
+            const int64_t chunk_tok = (T + sp - 1) / sp;
+            if (sp > 1 && chunk_tok < 256) break;
+            const int64_t waves = (streams * sp + slots - 1) / slots;
+            const double cost = (double)waves * (double)(chunk_tok + 384);
+            if (cost < best * 0.999) {
+                best = cost;
+                splits = sp;
+            }
+        }
     }
     int64_t chunk = (T + splits - 1) / splits;
     constexpr int64_t q = 64;   // chunk granularity (tokens)
