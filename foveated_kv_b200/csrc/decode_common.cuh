@@ -71,6 +71,13 @@ __device__ __forceinline__ uint32_t nib2_to_h2(uint32_t x) {
     return h2_as_u32(__hsub2(u32_as_h2(magic), u32_as_h2(0x64006400u)));
 }
 
+// high nibbles (x bits 4-7 and 20-23) -> f16x2 codes, exact and shift-free:
+// 0x5400 is 64 with a mantissa step of 1/16, so 0x5400 | (c << 4) is 64 + c.
+__device__ __forceinline__ uint32_t nib2hi_to_h2(uint32_t x) {
+    const uint32_t magic = (x & 0x00F000F0u) | 0x54005400u;
+    return h2_as_u32(__hsub2(u32_as_h2(magic), u32_as_h2(0x54005400u)));
+}
+
 // dequant v = code * scale + zero in fp16 arithmetic (two roundings, as the
 // reference's _dequant_int4_per_token does in fp16)
 __device__ __forceinline__ uint32_t dq_h2(uint32_t codes, uint32_t s2, uint32_t z2) {

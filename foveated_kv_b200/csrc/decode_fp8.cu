@@ -59,9 +59,11 @@ struct RecLayout {
     static constexpr int SIZE = 40 + 8 * D;   // floats
 };
 
+// q A-fragments of the CTA's head group, one uint4 per (k-step, lane), built
+// once by consumer warp 0 into shared memory and read by every consumer warp
 template <int D>
 __device__ __forceinline__ void build_q_frags(const DecodeParams& p, int s, int hg, int lane,
-                                              uint32_t (&qa)[D / 16][4]) {
+                                              uint4* __restrict__ qs) {
     const int r = lane >> 2, c = lane & 3;
     const int b = s / p.Hk, h = s % p.Hk;
     const int g = hg * kHeadsPerTile + r;
@@ -91,10 +93,10 @@ __device__ __forceinline__ void build_q_frags(const DecodeParams& p, int s, int 
             hi[e] = __float2half_rn(qv[4 * j + e]);
             lo[e] = __float2half_rn(qv[4 * j + e] - __half2float(hi[e]));
         }
-        qa[j][0] = h2_as_u32(__halves2half2(hi[0], hi[1]));
-        qa[j][1] = h2_as_u32(__halves2half2(lo[0], lo[1]));
-        qa[j][2] = h2_as_u32(__halves2half2(hi[2], hi[3]));
-        qa[j][3] = h2_as_u32(__halves2half2(lo[2], lo[3]));
+        qs[j * 32 + lane] = make_uint4(h2_as_u32(__halves2half2(hi[0], hi[1])),
+                                       h2_as_u32(__halves2half2(lo[0], lo[1])),
+                                       h2_as_u32(__halves2half2(hi[2], hi[3])),
+                                       h2_as_u32(__halves2half2(lo[2], lo[3])));
     }
 }
 
@@ -104,7 +106,7 @@ __device__ __forceinline__ void build_q_frags(const DecodeParams& p, int s, int 
 // [K rows | V rows]; far stages carry 128 tokens, near / decode stages 64.
 constexpr int kConsumerWarps = 4;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
-constexpr int kStages = 3;
+constexpr int kStages = 2;
 
 template <int D>
 struct Ring {
@@ -112,7 +114,9 @@ struct Ring {
     static constexpr int NEAR_TOK = 64;
     static constexpr int VOFF = NEAR_TOK * D * 2;        // K region (max of near / far)
     static constexpr int SLOT = VOFF + NEAR_TOK * D * 2;  // + V region
-    static constexpr int BYTES = kStages * SLOT + 2 * kStages * 8;
+    static constexpr int QOFF = kStages * SLOT;                 // q fragments
+    static constexpr int BAROFF = QOFF + (D / 16) * 32 * 16;    // mbarriers
+    static constexpr int BYTES = BAROFF + 2 * kStages * 8;
 };
 
 struct Segs {
@@ -141,7 +145,7 @@ __device__ __forceinline__ void stage_at(const Segs& sg, int k, int& seg, int& s
 template <int D>
 __device__ __forceinline__ void fp16_tile(const uint8_t* __restrict__ kbuf,
                                           const uint8_t* __restrict__ vbuf, int u0, int cnt,
-                                          int lane, const uint32_t (&qa)[D / 16][4],
+                                          int lane, const uint4* __restrict__ qs,
                                           WarpState<D>& st) {
     constexpr int KW = D / 8;      // u32 words per lane K chunk (D/4 halves)
     constexpr int VW = D / 16;     // u32 words per lane V chunk (D/8 halves)
@@ -172,8 +176,10 @@ __device__ __forceinline__ void fp16_tile(const uint8_t* __restrict__ kbuf,
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int j = 0; j < D / 16; ++j) {
-        mma16816(sc[0], qa[j], kr[0][2 * j], kr[0][2 * j + 1]);
-        mma16816(sc[1], qa[j], kr[1][2 * j], kr[1][2 * j + 1]);
+        const uint4 qv = qs[j * 32 + lane];
+        const uint32_t qa[4] = {qv.x, qv.y, qv.z, qv.w};
+        mma16816(sc[0], qa, kr[0][2 * j], kr[0][2 * j + 1]);
+        mma16816(sc[1], qa, kr[1][2 * j], kr[1][2 * j + 1]);
     }
     float s[4], pr[4];
 #pragma unroll
@@ -232,7 +238,7 @@ template <int D, int VG, int NT>
 __device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
                                           const uint8_t* __restrict__ vbuf, const int (&u0)[NT],
                                           int cnt, int gbase, int lane,
-                                          const uint32_t (&qa)[D / 16][4],
+                                          const uint4* __restrict__ qs,
                                           const uint32_t (&sz)[NT][4], WarpState<D>& st) {
     constexpr int KW = D / 16;    // u32 words of fp8 K per lane per token (D/4 bytes)
     constexpr int VB = D / 16;    // bytes of INT4 V per lane per token (D/8 dims)
@@ -279,13 +285,15 @@ __device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
         for (int n = 0; n < 2; ++n) sc[t][n][0] = sc[t][n][1] = sc[t][n][2] = sc[t][n][3] = 0.f;
 #pragma unroll
     for (int j = 0; j < D / 16; ++j) {
+        const uint4 qv = qs[j * 32 + lane];
+        const uint32_t qa[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
 #pragma unroll
             for (int n = 0; n < 2; ++n) {
                 uint32_t b0, b1;
                 e4m3x4_to_h2x2(kr[t][n][j], b0, b1);
-                mma16816(sc[t][n], qa[j], b0, b1);
+                mma16816(sc[t][n], qa, b0, b1);
             }
         }
     }
@@ -327,9 +335,9 @@ __device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
                 const uint32_t xcd = prmt(vr[t][2][wi], vr[t][3][wi], sel);
                 uint32_t a[4];
                 a[0] = nib2_to_h2(xab);
-                a[1] = nib2_to_h2(xab >> 4);
+                a[1] = nib2hi_to_h2(xab);
                 a[2] = nib2_to_h2(xcd);
-                a[3] = nib2_to_h2(xcd >> 4);
+                a[3] = nib2hi_to_h2(xcd);
                 mma16816(st.o[i], a, pb0, pb1);
             }
         } else {
@@ -347,9 +355,9 @@ __device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
                 const uint32_t xcd = prmt(vr[t][2][wi], vr[t][3][wi], sel);
                 uint32_t a[4];
                 a[0] = dq_h2(nib2_to_h2(xab), sAB, zAB);
-                a[1] = dq_h2(nib2_to_h2(xab >> 4), sAB, zAB);
+                a[1] = dq_h2(nib2hi_to_h2(xab), sAB, zAB);
                 a[2] = dq_h2(nib2_to_h2(xcd), sCD, zCD);
-                a[3] = dq_h2(nib2_to_h2(xcd >> 4), sCD, zCD);
+                a[3] = dq_h2(nib2hi_to_h2(xcd), sCD, zCD);
                 mma16816(st.o[i], a, pb0, pb1);
             }
         }
@@ -419,11 +427,12 @@ __device__ __forceinline__ void merge_and_emit(const DecodeParams& p, const floa
 }
 
 template <int D, int VG>
-__global__ void __launch_bounds__(kThreads, 2) decode_fp8_kernel(const DecodeParams p) {
+__global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodeParams p) {
     using R = RecLayout<D>;
     using RG = Ring<D>;
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * RG::SLOT);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + RG::BAROFF);
+    uint4* qs = reinterpret_cast<uint4*>(smem + RG::QOFF);
     uint64_t* empty = full + kStages;
     __shared__ int sh_last;
     const int split = blockIdx.x, hg = blockIdx.y, s = blockIdx.z;
@@ -490,8 +499,8 @@ __global__ void __launch_bounds__(kThreads, 2) decode_fp8_kernel(const DecodePar
     }
 
     // ---------------- consumer warps
-    uint32_t qa[D / 16][4];
-    build_q_frags<D>(p, s, hg, lane, qa);
+    if (w == 0) build_q_frags<D>(p, s, hg, lane, qs);
+    named_sync(1, kConsumerThreads);
     WarpState<D> st;
     st.init();
     const int64_t srow0 = (int64_t)s * p.F;
@@ -522,14 +531,14 @@ __global__ void __launch_bounds__(kThreads, 2) decode_fp8_kernel(const DecodePar
         if (seg == 1) {
             if (w + 4 < ntile) {
                 const int u0[2] = {w * kTile, (w + 4) * kTile};
-                far_tiles<D, VG, 2>(kbuf, vbuf, u0, cnt, start, lane, qa, szc, st);
+                far_tiles<D, VG, 2>(kbuf, vbuf, u0, cnt, start, lane, qs, szc, st);
             } else if (w < ntile) {
                 const int u0[1] = {w * kTile};
                 const uint32_t (&sz1)[1][4] = *reinterpret_cast<const uint32_t (*)[1][4]>(&szc[0]);
-                far_tiles<D, VG, 1>(kbuf, vbuf, u0, cnt, start, lane, qa, sz1, st);
+                far_tiles<D, VG, 1>(kbuf, vbuf, u0, cnt, start, lane, qs, sz1, st);
             }
         } else if (w < ntile) {
-            fp16_tile<D>(kbuf, vbuf, w * kTile, cnt, lane, qa, st);
+            fp16_tile<D>(kbuf, vbuf, w * kTile, cnt, lane, qs, st);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + slot);
