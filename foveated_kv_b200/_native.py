@@ -67,6 +67,8 @@ SIGNATURES = {
                                  P, P, SZ, P]),
     "fkv_decode_turbo": (C.c_int, [C.POINTER(DecodeShape), P, P, P, P, P, P, P, P, P, P, P,
                                    P, P, P, P, P, P, P, P, SZ, P]),
+    "fkv_decode_fp8_noalloc": (C.c_int, [C.POINTER(DecodeShape), P, P, P, P, P, P, P, P, P, P,
+                                         P, P, P, P]),
     "fkv_decode_fp8_partial": (C.c_int, [C.POINTER(DecodeShape), P, P, P, P, P, P, P, P, P,
                                          P, I32, P, P, P, SZ, P]),
     "fkv_combine_partials": (C.c_int, [I32, I32, I32, P, P, C.c_float, P, P, P, P]),

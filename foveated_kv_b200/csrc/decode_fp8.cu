@@ -15,6 +15,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <mutex>
 #include <utility>
 #include <vector>
 
@@ -885,3 +886,67 @@ int fkv_combine_partials(int32_t P, int32_t N, int32_t D, const float* parts,
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of fkv_decode_fp8
+// ---------------------------------------------------------------------------
+// Some callers cannot allocate device memory at the point where they decode:
+// code running under an allocator that is locked or owned by someone else
+// (an inference server's pre-planned memory pool, a plugin host that hands
+// out only the tensors it manages), or a runtime that forbids cudaMalloc on
+// the decode path.  For them the split-K scratch lives in this fixed
+// file-scope device array instead of a caller workspace.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 16u << 20;   // 16 MiB per GPU, held until exit
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+void* g_scratch_ptr[kMaxDevices] = {};
+std::mutex g_scratch_mu;
+
+// Device address of the scratch array on the current device.  The array's
+// host-side name is only a stand-in: the address must come from
+// cudaGetSymbolAddress, queried once per device with that device current.
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    FKV_CUDA_CHECK(cudaGetDevice(&dev));
+    FKV_REQUIRE(dev >= 0 && dev < kMaxDevices, FKV_ERR_UNSUPPORTED, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if (g_scratch_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        FKV_CUDA_CHECK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        g_scratch_ptr[dev] = p;
+    }
+    *out = g_scratch_ptr[dev];
+    return FKV_OK;
+}
+
+}  // namespace
+
+extern "C" int fkv_decode_fp8_noalloc(const FkvDecodeShape* sh, const uint16_t* near_k,
+                                      const uint16_t* near_v, const int32_t* near_valid,
+                                      const uint8_t* far_k, const uint8_t* far_v,
+                                      const uint16_t* v_scale, const uint16_t* v_zero,
+                                      const uint16_t* q, const uint16_t* dec_k,
+                                      const uint16_t* dec_v, uint16_t* out, int32_t* flags,
+                                      int32_t* tokens, void* stream) {
+    fkv::clear_error();
+    int rc = validate(sh);
+    if (rc) return rc;
+    const Plan pl = make_plan(sh);
+    const size_t need = pl.rec_bytes + pl.ticket_bytes + 256;
+    FKV_REQUIRE(need <= kNoAllocScratchBytes, FKV_ERR_INVALID,
+                "fkv_decode_fp8_noalloc: shape needs %zu scratch bytes, above the fixed "
+                "%zu-byte limit; use fkv_decode_fp8 with a caller workspace",
+                need, kNoAllocScratchBytes);
+    void* scratch = nullptr;
+    rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    // the array keeps the previous call's contents: zero the status word and
+    // split counters (the front of the scratch) before this call uses them
+    FKV_CUDA_CHECK(cudaMemsetAsync(scratch, 0, pl.ticket_bytes, (cudaStream_t)stream));
+    return fkv_decode_fp8(sh, near_k, near_v, near_valid, far_k, far_v, v_scale, v_zero, q,
+                          dec_k, dec_v, out, flags, tokens, scratch, kNoAllocScratchBytes,
+                          stream);
+}

@@ -171,6 +171,24 @@ int fkv_decode_turbo(const FkvDecodeShape* s, const uint16_t* near_k, const uint
                      const uint16_t* dec_v, uint16_t* out, int32_t* flags, int32_t* tokens,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* Same as fkv_decode_fp8, but allocation-free for callers that cannot call
+ * cudaMalloc on their decode path (a pre-planned memory pool owned by a
+ * serving runtime, a plugin host that only lends out its own tensors).  No
+ * counterpart in the reference (its Metal path has no caller workspace).
+ * The split scratch is a fixed 16 MiB device array inside libfkv.so, held by
+ * every GPU that loads the library until exit; shapes needing more (see
+ * fkv_decode_workspace_bytes) are rejected with FKV_ERR_INVALID.  The first
+ * call on a device looks up the array's device address, so make that first
+ * call before any stream capture.  All calls share the array (it keeps the
+ * last call's contents; each call zeroes the counters it needs): calls that
+ * overlap on the GPU race. */
+int fkv_decode_fp8_noalloc(const FkvDecodeShape* s, const uint16_t* near_k,
+                           const uint16_t* near_v, const int32_t* near_valid,
+                           const uint8_t* far_k, const uint8_t* far_v, const uint16_t* v_scale,
+                           const uint16_t* v_zero, const uint16_t* q, const uint16_t* dec_k,
+                           const uint16_t* dec_v, uint16_t* out, int32_t* flags,
+                           int32_t* tokens, void* stream);
+
 /* Sequence-split variant (no reference counterpart; the reference has no
  * multi-device code): same attention over this shard's tiers, but instead of
  * the final output writes one partial record per (b, q head):
