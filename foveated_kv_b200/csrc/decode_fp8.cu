@@ -49,9 +49,21 @@ struct DecodeParams {
     float* ws;            // split records
     int32_t* tickets;     // one counter per (stream, head group)
     int32_t* status;      // sticky kernel status word (0 = ok)
+    // TurboQuant far tier (far_k = 2-bit key codes, far_v = 2-bit value codes,
+    // v_scale = per-32-dim value scales)
+    const uint8_t* k_signs;
+    const uint16_t* k_norm;
+    const uint16_t* k_gamma;
+    const float* centroids;
+    const float* qproj;   // (B*Hq, 2D) f32: q Pi^T | q S^T, written by turbo_qproj_kernel
+    const float* turbo_pi;
+    const float* turbo_s;
+    float qjl_coef;
     int B, Hq, Hk, G, HG, Np, F, n_dec, dec_stride, splits, chunk;
     float margin, qscale;
 };
+
+constexpr int kTurbo = -1;   // VG value selecting the TurboQuant far tier
 
 // record = merged state of up to 8 q heads over a token range
 template <int D>
@@ -109,14 +121,16 @@ constexpr int kConsumerWarps = 4;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kStages = 2;
 
-template <int D>
+template <int D, int VG = 0>
 struct Ring {
     static constexpr int FAR_TOK = 128;
     static constexpr int NEAR_TOK = 64;
     static constexpr int VOFF = NEAR_TOK * D * 2;        // K region (max of near / far)
     static constexpr int SLOT = VOFF + NEAR_TOK * D * 2;  // + V region
-    static constexpr int QOFF = kStages * SLOT;                 // q fragments
-    static constexpr int BAROFF = QOFF + (D / 16) * 32 * 16;    // mbarriers
+    static constexpr int QFRAG = (D / 16) * 32 * 16;            // one set of q fragments
+    static constexpr int QOFF = kStages * SLOT;                 // q (+ turbo q Pi^T, q S^T)
+    static constexpr int TSUM = QOFF + (VG == kTurbo ? 3 : 1) * QFRAG;   // turbo row sums
+    static constexpr int BAROFF = TSUM + (VG == kTurbo ? 64 : 0);        // mbarriers
     static constexpr int BYTES = BAROFF + 2 * kStages * 8;
 };
 
@@ -365,6 +379,202 @@ __device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
     }
 }
 
+// ---------------------------------------------------------------------------
+// TurboQuant far tier: scores directly on codes
+// ---------------------------------------------------------------------------
+// far score = (|k| * <q Pi^T, c[idx]> + qjl_coef/D * gamma * <q S^T, sign>) / sqrt(D)
+// (foveated_attn.metal:486-521,684-688).  c[idx] is written as a thermometer
+// sum c0 + (c1-c0)[idx>=1] + (c2-c1)[idx>=2] + (c3-c2)[idx>=3] and sign as
+// 2[bit] - 1, so the tensor cores only see {0, 1} B fragments (exact in f16)
+// against hi/lo-split q Pi^T and q S^T fragments; the centroids and sums are
+// applied to the fp32 results.  Turbo K dimension permutation: k-step j, lane
+// c covers dims 4(4j+c) .. 4(4j+c)+3 = code byte 4j+c of the token row.
+
+// q Pi^T and q S^T for every (b, q head), f32 (the reference does these two
+// products with host matmuls, foveated_attn.cpp:419-421)
+template <int D>
+__global__ void turbo_qproj_kernel(const uint16_t* __restrict__ q, const float* __restrict__ Pi,
+                                   const float* __restrict__ Sm, float* __restrict__ out) {
+    __shared__ float qv[D];
+    const int bh = blockIdx.x;
+    for (int i = threadIdx.x; i < D; i += blockDim.x)
+        qv[i] = __half2float(__ushort_as_half(q[(int64_t)bh * D + i]));
+    __syncthreads();
+    for (int o = threadIdx.x; o < 2 * D; o += blockDim.x) {
+        const float* row = (o < D ? Pi + (int64_t)o * D : Sm + (int64_t)(o - D) * D);
+        float acc = 0.f;
+        for (int i = 0; i < D; ++i) acc = fmaf(qv[i], __ldg(row + i), acc);
+        out[(int64_t)bh * 2 * D + o] = acc;
+    }
+}
+
+// hi/lo fragments of q Pi^T and q S^T in the turbo permutation + per-head sums
+template <int D>
+__device__ __forceinline__ void build_turbo_frags(const DecodeParams& p, int s, int hg, int lane,
+                                                  uint4* __restrict__ qr, uint4* __restrict__ qk,
+                                                  float* __restrict__ sums) {
+    const int r = lane >> 2, c = lane & 3;
+    const int b = s / p.Hk, h = s % p.Hk;
+    const int g = hg * kHeadsPerTile + r;
+    const float* src = g < p.G ? p.qproj + ((int64_t)b * p.Hq + (int64_t)h * p.G + g) * 2 * D : nullptr;
+    float sr = 0.f, sk = 0.f;
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+        uint4* dst = which ? qk : qr;
+#pragma unroll
+        for (int j = 0; j < D / 16; ++j) {
+            __half hi[4], lo[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float v = src ? __ldg(src + which * D + 4 * (4 * j + c) + e) : 0.f;
+                if (which) sk += v; else sr += v;
+                hi[e] = __float2half_rn(v);
+                lo[e] = __float2half_rn(v - __half2float(hi[e]));
+            }
+            dst[j * 32 + lane] = make_uint4(h2_as_u32(__halves2half2(hi[0], hi[1])),
+                                            h2_as_u32(__halves2half2(lo[0], lo[1])),
+                                            h2_as_u32(__halves2half2(hi[2], hi[3])),
+                                            h2_as_u32(__halves2half2(lo[2], lo[3])));
+        }
+    }
+    sr = quad_sum(sr);
+    sk = quad_sum(sk);
+    if (c == 0) {
+        sums[r] = sr;
+        sums[8 + r] = sk;
+    }
+}
+
+// norm | gamma << 16 and the value group scale of the lane's 4 PV tokens
+template <int D>
+__device__ __forceinline__ void load_turbo_sz(const DecodeParams& p, int64_t srow0, int start,
+                                              int u0, int cnt, int lane, uint32_t (&ng)[4],
+                                              uint32_t (&vs)[2]) {
+    const int r = lane >> 2, c = lane & 3;
+    const int grp = (r * (D / 8)) / 32;
+    uint16_t sv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int u = u0 + (e >> 1) * 8 + 2 * c + (e & 1);
+        if (u < cnt) {
+            const int64_t row = srow0 + start + u;
+            ng[e] = (uint32_t)__ldg(p.k_norm + row) | ((uint32_t)__ldg(p.k_gamma + row) << 16);
+            sv[e] = __ldg(p.v_scale + row * (D / 32) + grp);
+        } else {
+            ng[e] = 0u;
+            sv[e] = 0;
+        }
+    }
+    vs[0] = (uint32_t)sv[0] | ((uint32_t)sv[1] << 16);
+    vs[1] = (uint32_t)sv[2] | ((uint32_t)sv[3] << 16);
+}
+
+// {0,1} f16 pairs: bit 0 and bit 16 of x -> 0x3C00 (1.0) in the matching half
+__device__ __forceinline__ uint32_t bits2_to_h2(uint32_t x) { return (x & 0x00010001u) * 0x3C00u; }
+
+template <int D>
+__device__ __forceinline__ void turbo_tile(const DecodeParams& p, const uint8_t* __restrict__ kbuf,
+                                           const uint8_t* __restrict__ vbuf, int u0, int cnt,
+                                           int64_t srow0, int gbase, int lane,
+                                           const uint4* __restrict__ qr,
+                                           const uint4* __restrict__ qk, const float (&cf)[6],
+                                           float sum_r, float sum_k, const uint32_t (&ng)[4],
+                                           const uint32_t (&vsc)[2], WarpState<D>& st) {
+    constexpr int IW = D / 16;    // u32 words of 2-bit key codes per token (D/4 bytes)
+    constexpr int SB = D / 8;     // sign bytes per token
+    const int r = lane >> 2, c = lane & 3;
+    uint32_t kr[2][IW];
+    uint32_t sg[2][SB / 4];
+#pragma unroll
+    for (int n = 0; n < 2; ++n) {
+        const int u = u0 + 8 * n + r;
+        const uint4* src = reinterpret_cast<const uint4*>(kbuf + u * (D / 4));
+#pragma unroll
+        for (int x = 0; x < IW / 4; ++x) {
+            const uint4 w4 = src[x];
+            kr[n][4 * x] = w4.x; kr[n][4 * x + 1] = w4.y; kr[n][4 * x + 2] = w4.z; kr[n][4 * x + 3] = w4.w;
+        }
+        const bool ok = u < cnt;
+        const uint32_t* gs = reinterpret_cast<const uint32_t*>(p.k_signs + (srow0 + gbase + u) * SB);
+#pragma unroll
+        for (int x = 0; x < SB / 4; ++x) sg[n][x] = ok ? __ldg(gs + x) : 0u;
+    }
+    float acc[4][2][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int n = 0; n < 2; ++n) acc[a][n][0] = acc[a][n][1] = acc[a][n][2] = acc[a][n][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < D / 16; ++j) {
+        const uint4 rv = qr[j * 32 + lane];
+        const uint4 kv = qk[j * 32 + lane];
+        const uint32_t ar[4] = {rv.x, rv.y, rv.z, rv.w};
+        const uint32_t ak[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+            const uint32_t x = (kr[n][j] >> (8 * c)) & 0xFFu;   // codes of dims 4(4j+c)+0..3
+            const uint32_t y01 = x | (x << 14);                 // dim0 -> bits 0-1, dim1 -> 16-17
+            const uint32_t y23 = (x >> 4) | (x << 10);          // dim2 -> bits 0-1, dim3 -> 16-17
+            mma16816(acc[0][n], ar, bits2_to_h2(y01 | (y01 >> 1)), bits2_to_h2(y23 | (y23 >> 1)));
+            mma16816(acc[1][n], ar, bits2_to_h2(y01 >> 1), bits2_to_h2(y23 >> 1));
+            mma16816(acc[2][n], ar, bits2_to_h2(y01 & (y01 >> 1)), bits2_to_h2(y23 & (y23 >> 1)));
+            const int sbyte = 2 * j + (c >> 1);                  // sign byte of these dims
+            const uint32_t z = (sg[n][sbyte >> 2] >> (8 * (sbyte & 3) + 4 * (c & 1))) & 0xFu;
+            mma16816(acc[3][n], ak, bits2_to_h2(z | (z << 15)), bits2_to_h2((z >> 2) | (z << 13)));
+        }
+    }
+    float s[4], pr[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int u = u0 + (j >> 1) * 8 + 2 * c + (j & 1);
+        const int n = j >> 1, e = j & 1;
+        const float t1 = acc[0][n][e] + acc[0][n][2 + e];
+        const float t2 = acc[1][n][e] + acc[1][n][2 + e];
+        const float t3 = acc[2][n][e] + acc[2][n][2 + e];
+        const float sgn = acc[3][n][e] + acc[3][n][2 + e];
+        const float2 f = __half22float2(u32_as_h2(ng[j]));      // (norm, gamma)
+        const float mse = fmaf(cf[3], t3, fmaf(cf[2], t2, fmaf(cf[1], t1, cf[0] * sum_r)));
+        const float qjl = cf[4] * f.y * fmaf(2.f, sgn, -sum_k);
+        const float v = fmaf(f.x, mse, qjl) * cf[5];
+        s[j] = u < cnt ? v : -INFINITY;
+        if (u < cnt && v > st.mf) {
+            st.mf = v;
+            st.af = gbase + u;
+        }
+    }
+    st.softmax_step(s, pr, lane);
+    const uint32_t pb0 = pack_h2(pr[0], pr[1]);
+    const uint32_t pb1 = pack_h2(pr[2], pr[3]);
+    // value levels {-1, -1/3, 1/3, 1} as f16, selected by prmt
+    const uint32_t lut0 = h2_as_u32(__floats2half2_rn(-1.f, -1.f / 3.f));
+    const uint32_t lut1 = h2_as_u32(__floats2half2_rn(1.f / 3.f, 1.f));
+    uint32_t vw[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int u = u0 + (e >> 1) * 8 + 2 * c + (e & 1);
+        const uint8_t* src = vbuf + u * (D / 4) + r * (D / 32);
+        if constexpr (D == 128) vw[e] = u < cnt ? *reinterpret_cast<const uint32_t*>(src) : 0u;
+        else vw[e] = u < cnt ? (uint32_t)*reinterpret_cast<const uint16_t*>(src) : 0u;
+    }
+#pragma unroll
+    for (int i = 0; i < D / 16; ++i) {
+        const int sh = 8 * (i >> 1) + 4 * (i & 1);
+        uint32_t a[4];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {        // tokens (A,B) then (C,D)
+#pragma unroll
+            for (int dd = 0; dd < 2; ++dd) {           // dim d0 then d1
+                const uint32_t ca = (vw[2 * half] >> (sh + 2 * dd)) & 3u;
+                const uint32_t cb = (vw[2 * half + 1] >> (sh + 2 * dd)) & 3u;
+                const uint32_t sel = (ca | (cb << 8)) * 0x22u + 0x1010u;
+                const uint32_t lv = prmt(lut0, lut1, sel);
+                a[2 * half + dd] = h2_as_u32(__hmul2(u32_as_h2(lv), u32_as_h2(vsc[half])));
+            }
+        }
+        mma16816(st.o[i], a, pb0, pb1);
+    }
+}
+
 // merge `n` records (strided by `stride` floats) into the caller's registers:
 // each thread handles (head, d) pairs e = tid, tid+nthreads, ...
 template <int D>
@@ -430,7 +640,7 @@ __device__ __forceinline__ void merge_and_emit(const DecodeParams& p, const floa
 template <int D, int VG>
 __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodeParams p) {
     using R = RecLayout<D>;
-    using RG = Ring<D>;
+    using RG = Ring<D, VG>;
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + RG::BAROFF);
     uint4* qs = reinterpret_cast<uint4*>(smem + RG::QOFF);
@@ -481,7 +691,11 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
                 uint8_t* dst = smem + slot * RG::SLOT;
                 const uint8_t *ks, *vs;
                 uint32_t kb, vb;
-                if (seg == 1) {
+                if (seg == 1 && VG == kTurbo) {
+                    ks = p.far_k + ((int64_t)s * p.F + start) * (D / 4);   // 2-bit key codes
+                    vs = p.far_v + ((int64_t)s * p.F + start) * (D / 4);   // 2-bit value codes
+                    kb = vb = cnt * (D / 4);
+                } else if (seg == 1) {
                     ks = fk + (int64_t)start * D;
                     vs = fv + (int64_t)start * (D / 2);
                     kb = cnt * D;
@@ -500,27 +714,50 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
     }
 
     // ---------------- consumer warps
-    if (w == 0) build_q_frags<D>(p, s, hg, lane, qs);
+    uint4* qr = qs + RG::QFRAG / 16;
+    uint4* qk = qr + RG::QFRAG / 16;
+    float* tsum = reinterpret_cast<float*>(smem + RG::TSUM);
+    if (w == 0) {
+        build_q_frags<D>(p, s, hg, lane, qs);
+        if constexpr (VG == kTurbo) build_turbo_frags<D>(p, s, hg, lane, qr, qk, tsum);
+    }
     named_sync(1, kConsumerThreads);
+    float cf[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float sum_r = 0.f, sum_k = 0.f;
+    if constexpr (VG == kTurbo) {
+        const float c0 = __ldg(p.centroids), c1 = __ldg(p.centroids + 1);
+        const float c2 = __ldg(p.centroids + 2), c3 = __ldg(p.centroids + 3);
+        cf[0] = c0; cf[1] = c1 - c0; cf[2] = c2 - c1; cf[3] = c3 - c2;
+        cf[4] = p.qjl_coef / (float)D;
+        cf[5] = p.qscale;
+        sum_r = tsum[lane >> 2];
+        sum_k = tsum[8 + (lane >> 2)];
+    }
     WarpState<D> st;
     st.init();
     const int64_t srow0 = (int64_t)s * p.F;
     uint32_t szc[2][4], szn[2][4];
-    auto prefetch = [&](int k, uint32_t (&dst)[2][4]) {
+    uint32_t vsc[2][2], vsn[2][2];   // turbo: value group scales
+    auto prefetch = [&](int k, uint32_t (&dst)[2][4], uint32_t (&vdst)[2][2]) {
         if (k >= nstage) return;
         int seg, start, cnt;
         stage_at<D>(sg, k, seg, start, cnt);
         if (seg != 1) return;
 #pragma unroll
-        for (int x = 0; x < 2; ++x) load_sz<D, VG>(p, srow0, start, (w + 4 * x) * kTile, cnt, lane, dst[x]);
+        for (int x = 0; x < 2; ++x) {
+            if constexpr (VG == kTurbo)
+                load_turbo_sz<D>(p, srow0, start, (w + 4 * x) * kTile, cnt, lane, dst[x], vdst[x]);
+            else
+                load_sz<D, VG>(p, srow0, start, (w + 4 * x) * kTile, cnt, lane, dst[x]);
+        }
     };
-    prefetch(0, szc);
+    prefetch(0, szc, vsc);
     int failed_at = -1;
     for (int k = 0; k < nstage; ++k) {
         const int slot = k % kStages;
         int seg, start, cnt;
         stage_at<D>(sg, k, seg, start, cnt);
-        prefetch(k + 1, szn);
+        prefetch(k + 1, szn, vsn);
         if (!mbar_wait(full + slot, (k / kStages) & 1)) {
             atomicExch(p.status, FKV_ERR_TIMEOUT);
             failed_at = k;
@@ -529,7 +766,16 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
         const uint8_t* kbuf = smem + slot * RG::SLOT;
         const uint8_t* vbuf = kbuf + RG::VOFF;
         const int ntile = (cnt + kTile - 1) / kTile;
-        if (seg == 1) {
+        if (seg == 1 && VG == kTurbo) {
+#pragma unroll
+            for (int x = 0; x < 2; ++x) {
+                const int i = w + 4 * x;
+                if (i < ntile)
+                    turbo_tile<D>(p, kbuf, vbuf, i * kTile, cnt, srow0, start, lane, qr, qk, cf,
+                                  sum_r, sum_k, szc[x], vsc[x], st);
+            }
+        } else if (seg == 1) {
+          if constexpr (VG != kTurbo) {
             if (w + 4 < ntile) {
                 const int u0[2] = {w * kTile, (w + 4) * kTile};
                 far_tiles<D, VG, 2>(kbuf, vbuf, u0, cnt, start, lane, qs, szc, st);
@@ -538,15 +784,19 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
                 const uint32_t (&sz1)[1][4] = *reinterpret_cast<const uint32_t (*)[1][4]>(&szc[0]);
                 far_tiles<D, VG, 1>(kbuf, vbuf, u0, cnt, start, lane, qs, sz1, st);
             }
+          }
         } else if (w < ntile) {
             fp16_tile<D>(kbuf, vbuf, w * kTile, cnt, lane, qs, st);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + slot);
 #pragma unroll
-        for (int x = 0; x < 2; ++x)
+        for (int x = 0; x < 2; ++x) {
 #pragma unroll
             for (int e = 0; e < 4; ++e) szc[x][e] = szn[x][e];
+            vsc[x][0] = vsn[x][0];
+            vsc[x][1] = vsn[x][1];
+        }
     }
     if (failed_at >= 0) {
         // the producer runs at most kStages ahead of the consumers: wait
@@ -696,6 +946,7 @@ int num_sms() {
 struct Plan {
     int HG, splits, chunk;
     size_t rec_bytes, ticket_bytes;
+    size_t qproj_bytes;   // turbo only: (B*Hq, 2D) f32 after the counters
 };
 
 Plan make_plan(const FkvDecodeShape* sh) {
@@ -733,6 +984,7 @@ Plan make_plan(const FkvDecodeShape* sh) {
     const int D = sh->D;
     pl.rec_bytes = pl.splits > 1 ? (size_t)streams * pl.splits * (40 + 8 * D) * sizeof(float) : 0;
     pl.ticket_bytes = 16 + (size_t)streams * sizeof(int32_t);   // status word + counters
+    pl.qproj_bytes = (size_t)sh->B * sh->Hq * 2 * D * sizeof(float);
     return pl;
 }
 
@@ -773,9 +1025,11 @@ int launch_kernel(void (*kern)(DecodeParams), int smem, dim3 grid, const DecodeP
 }
 
 int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws_bytes,
-           cudaStream_t st) {
+           cudaStream_t st, bool turbo = false) {
     const Plan pl = make_plan(sh);
-    const size_t need = pl.rec_bytes + pl.ticket_bytes + 256;
+    const size_t qoff = (pl.ticket_bytes + 255) & ~(size_t)255;
+    const size_t front = turbo ? qoff + pl.qproj_bytes : pl.ticket_bytes;
+    const size_t need = pl.rec_bytes + front + 256;
     FKV_REQUIRE(workspace != nullptr && ws_bytes >= need, FKV_ERR_INVALID,
                 "workspace too small: %zu < %zu bytes", ws_bytes, need);
     FKV_REQUIRE(aligned16(workspace), FKV_ERR_INVALID, "workspace must be 16-byte aligned");
@@ -789,10 +1043,22 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     p.status = reinterpret_cast<int32_t*>(workspace);
     p.tickets = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(workspace) + 16);
     const size_t rec_off = (ws_bytes - pl.rec_bytes) & ~(size_t)255;
-    FKV_REQUIRE(rec_off >= pl.ticket_bytes, FKV_ERR_INVALID,
+    FKV_REQUIRE(rec_off >= front, FKV_ERR_INVALID,
                 "workspace too small for counters + records (%zu bytes)", ws_bytes);
     p.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + rec_off);
     dim3 grid(pl.splits, pl.HG, sh->B * sh->Hk);
+    if (turbo) {
+        float* qproj = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + qoff);
+        p.qproj = qproj;
+        if (sh->D == 128) {
+            turbo_qproj_kernel<128><<<sh->B * sh->Hq, 256, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj);
+            FKV_LAUNCH_CHECK();
+            return launch_kernel(decode_fp8_kernel<128, kTurbo>, Ring<128, kTurbo>::BYTES, grid, p, st);
+        }
+        turbo_qproj_kernel<64><<<sh->B * sh->Hq, 128, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj);
+        FKV_LAUNCH_CHECK();
+        return launch_kernel(decode_fp8_kernel<64, kTurbo>, Ring<64, kTurbo>::BYTES, grid, p, st);
+    }
     if (sh->D == 128) {
         if (sh->v_group == 0) return launch_kernel(decode_fp8_kernel<128, 0>, Ring<128>::BYTES, grid, p, st);
         return launch_kernel(decode_fp8_kernel<128, 32>, Ring<128>::BYTES, grid, p, st);
@@ -832,7 +1098,7 @@ extern "C" {
 size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s) {
     if (validate(s) != FKV_OK) return 0;
     const Plan pl = make_plan(s);
-    return pl.rec_bytes + pl.ticket_bytes + 256;
+    return pl.rec_bytes + pl.ticket_bytes + 256 + ((pl.qproj_bytes + 255) & ~(size_t)255) + 256;
 }
 
 int fkv_decode_fp8(const FkvDecodeShape* sh, const uint16_t* near_k, const uint16_t* near_v,
@@ -849,6 +1115,36 @@ int fkv_decode_fp8(const FkvDecodeShape* sh, const uint16_t* near_k, const uint1
     FKV_REQUIRE(out && flags && tokens, FKV_ERR_INVALID, "outputs are NULL");
     p.out = out; p.flags = flags; p.tokens = tokens;
     return launch(sh, p, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int fkv_decode_turbo(const FkvDecodeShape* sh, const uint16_t* near_k, const uint16_t* near_v,
+                     const int32_t* near_valid, const uint8_t* k_idx, const uint8_t* k_signs,
+                     const uint16_t* k_norm, const uint16_t* k_gamma, const uint8_t* v_packed,
+                     const uint16_t* v_scale, const float* Pi, const float* Smat,
+                     const float* centroids, const uint16_t* q, const uint16_t* dec_k,
+                     const uint16_t* dec_v, uint16_t* out, int32_t* flags, int32_t* tokens,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+    fkv::clear_error();
+    int rc = validate(sh);
+    if (rc) return rc;
+    FKV_REQUIRE(q && near_valid && Pi && Smat && centroids && out && flags && tokens,
+                FKV_ERR_INVALID, "fkv_decode_turbo: NULL argument");
+    FKV_REQUIRE(sh->n_near_alloc == 0 || (near_k && near_v), FKV_ERR_INVALID, "near is NULL");
+    FKV_REQUIRE(sh->n_far == 0 || (k_idx && k_signs && k_norm && k_gamma && v_packed && v_scale),
+                FKV_ERR_INVALID, "turbo far tier pointer is NULL");
+    FKV_REQUIRE(sh->n_dec == 0 || (dec_k && dec_v), FKV_ERR_INVALID, "decode buffer is NULL");
+    FKV_REQUIRE(aligned16(q) && aligned16(near_k) && aligned16(near_v) && aligned16(k_idx) &&
+                    aligned16(v_packed) && aligned16(dec_k) && aligned16(dec_v) &&
+                    ((uintptr_t)k_signs & 3u) == 0,
+                FKV_ERR_INVALID, "turbo tier / query pointers misaligned");
+    DecodeParams p{};
+    p.near_k = near_k; p.near_v = near_v; p.near_valid = near_valid;
+    p.far_k = k_idx; p.far_v = v_packed; p.v_scale = v_scale;
+    p.k_signs = k_signs; p.k_norm = k_norm; p.k_gamma = k_gamma; p.centroids = centroids;
+    p.turbo_pi = Pi; p.turbo_s = Smat; p.qjl_coef = sh->qjl_coef;
+    p.q = q; p.dec_k = dec_k; p.dec_v = dec_v;
+    p.out = out; p.flags = flags; p.tokens = tokens;
+    return launch(sh, p, workspace, workspace_bytes, (cudaStream_t)stream, true);
 }
 
 int fkv_decode_fp8_partial(const FkvDecodeShape* sh, const uint16_t* near_k,

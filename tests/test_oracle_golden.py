@@ -192,3 +192,12 @@ def test_combine_partials_matches_single_pass():
     out, fl, tok = O.combine_partials(m, l, o, inf, -inf, np.full((4, 3), -1), 0.5)
     p = np.exp(s - s.max(1, keepdims=True))
     assert np.allclose(out, (p @ v) / p.sum(1, keepdims=True))
+
+
+@pytest.mark.parametrize("d", [64, 128])
+def test_product_turbo_constants_match_reference(golden, d):
+    """The package's own host-side constants equal the reference's."""
+    from foveated_kv_b200.turbo_constants import host_constants
+    t = golden("turbo_constants.npz")
+    for k, v in zip(("Pi", "S", "centroids", "boundaries"), host_constants(d)):
+        assert np.array_equal(v, t[f"{k}_{d}"]), k
