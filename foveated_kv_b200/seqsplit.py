@@ -1,0 +1,140 @@
+"""Sequence-split decode across GPUs (long contexts; no reference counterpart:
+the reference has no multi-device code).
+
+The prefill sequence [0, S) is split evenly into world_size shards of
+positions.  Each rank tiers its shard with the GLOBAL recency tier boundaries
+(a position is near or far exactly as in the unsplit cache), runs the fused
+decode kernel in partial mode (one (m, l, o, min_near, max_far, argmax)
+record per (b, q head), argmax as a global far index), all-gathers the
+records over NCCL (NVLink), and merges them with fkv_combine_partials in
+rank order, so flags / tokens equal those of the unsplit cache.  The decode
+buffer lives on the last rank (it holds the sequence's tail).
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from . import _native
+from .cache import FoveatedLayer, _Workspace, _p, _stream, F16, I32, U8
+from .config import TierConfig
+
+
+def shard_bounds(S: int, rank: int, world: int):
+    """Even split of [0, S): shard `rank` is [lo, hi)."""
+    base, rem = divmod(S, world)
+    lo = rank * base + min(rank, rem)
+    return lo, lo + base + (1 if rank < rem else 0)
+
+
+def shard_positions(S: int, lo: int, hi: int, cfg: TierConfig):
+    """Global-tier near / far positions inside [lo, hi) and the global far
+    index of the shard's first far token."""
+    tb = cfg.tier_boundaries(S)
+    ns, w, ms, me, nms = tb["n_sinks"], tb["window"], tb["mid_start"], tb["mid_end"], tb["near_mid_start"]
+    seg = lambda a, b: np.arange(max(a, lo), min(b, hi), dtype=np.int32)
+    near = np.concatenate([seg(0, ns), seg(nms, me), seg(S - w, S)])
+    far = seg(ms, nms)
+    off = int(far[0] - ms) if far.size else 0
+    return near, far, off, tb
+
+
+def compress_shard(k_shard: torch.Tensor, v_shard: torch.Tensor, S: int, lo: int,
+                   cfg: TierConfig, keep_archive: bool = False) -> tuple:
+    """Tier one rank's shard (B, H, hi-lo, D) of a length-S prefill.
+    Returns (FoveatedLayer, far_index_offset)."""
+    lib = _native.load()
+    k = k_shard.to(F16).contiguous()
+    v = v_shard.to(F16).contiguous()
+    B, H, Ssh, D = k.shape
+    near, far, off, tb = shard_positions(S, lo, lo + Ssh, cfg)
+    R = near.size
+    Np = R + max(int(R * cfg.promo_headroom_pct), cfg.promo_headroom_min)
+    Fn = far.size
+    dev = k.device
+    L = _native.TierLayout()
+    L.S, L.n_near_padded, L.far_count, L.r_actual = Ssh, Np, Fn, R
+    near_idx = torch.full((B, H, Np), -1, dtype=I32, device=dev)
+    near_idx[:, :, :R] = torch.from_numpy(near - lo).to(dev)
+    far_idx_local = torch.from_numpy(far - lo).to(dev).expand(B, H, Fn).contiguous()
+    near_k = torch.empty((B, H, Np, D), dtype=F16, device=dev)
+    near_v = torch.empty_like(near_k)
+    far_k = torch.empty((B, H, Fn, D), dtype=U8, device=dev)
+    far_v = torch.empty((B, H, Fn, D // 2), dtype=U8, device=dev)
+    vg = cfg.v_group
+    sshape = (B, H, Fn) if vg is None else (B, H, Fn, D // vg)
+    vsc = torch.empty(sshape, dtype=F16, device=dev)
+    vze = torch.empty(sshape, dtype=F16, device=dev)
+    arc_k = torch.empty((B, H, Fn, D), dtype=F16, device=dev) if keep_archive else None
+    arc_v = torch.empty_like(arc_k) if keep_archive else None
+    _native.check(lib.fkv_compress_fp8(
+        C.byref(L), B, H, D, _p(k), _p(v), Ssh * D, _p(near_idx), _p(far_idx_local),
+        int(vg or 0), _p(near_k), _p(near_v), _p(far_k), _p(far_v), _p(vsc), _p(vze),
+        _p(arc_k), _p(arc_v), _stream(dev)), "fkv_compress_fp8")
+    near_idx[:, :, :R] += lo
+    lay = FoveatedLayer(near_k=near_k, near_v=near_v, near_idx=near_idx,
+                        near_valid=torch.full((B, H), R, dtype=I32, device=dev),
+                        far_idx=(far_idx_local + lo), archive_k=arc_k, archive_v=arc_v,
+                        far_k=far_k, far_v=far_v, far_v_scale=vsc, far_v_zero=vze,
+                        v_group=vg, spike_margin=cfg.spike_margin)
+    return lay, off
+
+
+def decode_partial(layer: FoveatedLayer, q: torch.Tensor, far_offset: int):
+    """This shard's partial records: part (B*Hq, D+4) f32, arg (B*Hq) int32."""
+    lib = _native.load()
+    B, Hq, D = q.shape[0], q.shape[1], q.shape[-1]
+    qq = q.reshape(B, Hq, D).to(F16).contiguous()
+    sh = layer._fill_shape(Hq, layer.spike_margin)
+    ws = _Workspace.get(lib.fkv_decode_workspace_bytes(C.byref(sh)), layer.device)
+    part = torch.empty((B * Hq, D + 4), dtype=torch.float32, device=layer.device)
+    arg = torch.empty((B * Hq,), dtype=I32, device=layer.device)
+    dk = layer._dec_k if layer.n_decode else None
+    dv = layer._dec_v if layer.n_decode else None
+    _native.check(lib.fkv_decode_fp8_partial(
+        C.byref(sh), _p(layer.near_k), _p(layer.near_v), _p(layer.near_valid), _p(layer.far_k),
+        _p(layer.far_v), _p(layer.far_v_scale), _p(layer.far_v_zero), _p(qq), _p(dk), _p(dv),
+        int(far_offset), _p(part), _p(arg), ws.data_ptr(), ws.numel(), _stream(layer.device)),
+        "fkv_decode_fp8_partial")
+    return part, arg
+
+
+def gather_partials(part: torch.Tensor, arg: torch.Tensor, group=None):
+    """All-gather every rank's records: (P, N, D+4) and (P, N), rank order.
+    NCCL over NVLink on GPUs; any backend works (gloo for host tests)."""
+    P = dist.get_world_size(group)
+    parts = torch.empty((P * part.shape[0],) + tuple(part.shape[1:]), dtype=part.dtype,
+                        device=part.device)
+    args = torch.empty((P * arg.shape[0],), dtype=arg.dtype, device=arg.device)
+    dist.all_gather_into_tensor(parts, part.contiguous(), group=group)
+    dist.all_gather_into_tensor(args, arg.contiguous(), group=group)
+    return parts.view((P,) + tuple(part.shape)), args.view(P, -1)
+
+
+def combine(parts: torch.Tensor, args: torch.Tensor, margin: float):
+    """Merge (P, N, D+4) records on the device: out (N, D) fp16, flags, tokens."""
+    lib = _native.load()
+    P, N, D4 = parts.shape
+    D = D4 - 4
+    out = torch.empty((N, D), dtype=F16, device=parts.device)
+    flags = torch.empty((N,), dtype=I32, device=parts.device)
+    tokens = torch.empty((N,), dtype=I32, device=parts.device)
+    _native.check(lib.fkv_combine_partials(P, N, D, _p(parts), _p(args), float(margin), _p(out),
+                                           _p(flags), _p(tokens), _stream(parts.device)),
+                  "fkv_combine_partials")
+    return out, flags, tokens
+
+
+def decode_seqsplit(layer: FoveatedLayer, q: torch.Tensor, far_offset: int, group=None):
+    """One decode step of a sequence-split layer: local partial, all-gather,
+    combine.  Returns (out (B, Hq, 1, D), flags (B, Hq), tokens (B, Hq))."""
+    B, Hq, D = q.shape[0], q.shape[1], q.shape[-1]
+    part, arg = decode_partial(layer, q, far_offset)
+    parts, args = gather_partials(part, arg, group)
+    out, fl, tk = combine(parts, args, layer.spike_margin)
+    return out.view(B, Hq, 1, D), fl.view(B, Hq), tk.view(B, Hq)

@@ -583,3 +583,58 @@ class DrainFilter:
                 out.append((layer, b, h, fl, pos))
                 self.stats["spikes_queued"] += 1
         return out
+
+
+def shard_tier_positions(S: int, lo: int, hi: int, tb: dict):
+    """Near / far positions of the global recency tiers that fall in the
+    shard [lo, hi) (sequence split; no reference counterpart).  Returns
+    (near_positions, far_positions, far_index_offset) with the far offset the
+    global far-local index of the shard's first far token."""
+    near, far = recency_indices(S, tb)
+    n = near[(near >= lo) & (near < hi)]
+    f = far[(far >= lo) & (far < hi)]
+    off = int(f[0] - tb["mid_start"]) if f.size else 0
+    return n.astype(np.int32), f.astype(np.int32), off
+
+
+def decode_partials(layer: dict, q: np.ndarray, dec_k=None, dec_v=None, far_offset: int = 0):
+    """Per (b, q head) partial softmax record of this tier shard:
+    m, l (sum exp(s - m)), o (sum exp(s - m) v, unnormalised), min_near,
+    max_far and its global far index (earliest on ties) or -1."""
+    q = np.asarray(q, dtype=np.float16)
+    B, Hq, D = q.shape
+    Hk = layer["near_k"].shape[1]
+    G = Hq // Hk
+    fk = e4m3_to_fp16(layer["far_k"])
+    fv = dequant_int4(layer["far_v"], layer["far_v_scale"], layer["far_v_zero"], layer.get("v_group"))
+    qs = prescaled_query(q).astype(np.float64)
+    N = B * Hq
+    m = np.full(N, -np.inf); l = np.zeros(N); o = np.zeros((N, D))
+    mn = np.full(N, np.inf); mf = np.full(N, -np.inf); arg = np.full(N, -1, dtype=np.int64)
+    for b in range(B):
+        for h in range(Hk):
+            nv = int(layer["near_valid"][b, h])
+            nk = layer["near_k"][b, h, :nv].astype(np.float64)
+            nvv = layer["near_v"][b, h, :nv].astype(np.float64)
+            if dec_k is not None and dec_k.shape[2] > 0:
+                nk = np.concatenate([nk, dec_k[b, h].astype(np.float64)])
+                nvv = np.concatenate([nvv, dec_v[b, h].astype(np.float64)])
+            qg = qs[b, h * G:(h + 1) * G]
+            sn = qg @ nk.T
+            sf = qg @ fk[b, h].astype(np.float64).T
+            sc = np.concatenate([sn, sf], axis=1)
+            vv = np.concatenate([nvv, fv[b, h].astype(np.float64)])
+            for g in range(G):
+                i = b * Hq + h * G + g
+                if sc.shape[1]:
+                    m[i] = sc[g].max()
+                    p = np.exp(sc[g] - m[i])
+                    l[i] = p.sum()
+                    o[i] = p @ vv
+                if sn.shape[1]:
+                    mn[i] = sn[g].min()
+                if sf.shape[1]:
+                    a = int(np.argmax(sf[g]))
+                    mf[i] = sf[g, a]
+                    arg[i] = a + far_offset
+    return m, l, o, mn, mf, arg

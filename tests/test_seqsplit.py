@@ -1,0 +1,135 @@
+"""Sequence-split decode: shard tiering, partial records and their merge.
+
+CPU (gloo, 2 ranks): the exchange step carries the oracle's per-shard partial
+records and the merged result equals the unsplit oracle attention.  GPU: the
+partial kernel + combine kernel over P shards on one device equal the unsplit
+fused decode; with >= 2 GPUs the NCCL path under torchrun as well."""
+
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import fkv_oracle as O
+from foveated_kv_b200.synthetic import numpy_workload
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _oracle_shard(w, S, lo, hi, cfg):
+    tb = O.tier_boundaries(S, **cfg)
+    near, far, off = O.shard_tier_positions(S, lo, hi, tb)
+    k, v = w["k"], w["v"]
+    B, H, _, D = k.shape
+    R = near.size
+    lay = {"near_k": k[:, :, near], "near_v": v[:, :, near],
+           "near_valid": np.full((B, H), R, np.int32), "far_k": O.fp16_to_e4m3(k[:, :, far]),
+           "v_group": None}
+    lay["far_v"], lay["far_v_scale"], lay["far_v_zero"] = O.quantize_int4(v[:, :, far])
+    return lay, off
+
+
+def test_shard_positions_partition_global_tiers():
+    from foveated_kv_b200.seqsplit import shard_bounds
+    S, cfg = 1000, dict(near_pct=0.05, window_size=32)
+    tb = O.tier_boundaries(S, **cfg)
+    near, far = O.recency_indices(S, tb)
+    for world in (1, 2, 3, 8):
+        ns, fs = [], []
+        for r in range(world):
+            lo, hi = shard_bounds(S, r, world)
+            n, f, off = O.shard_tier_positions(S, lo, hi, tb)
+            if f.size:
+                assert off == f[0] - tb["mid_start"]
+            ns.append(n); fs.append(f)
+        assert np.array_equal(np.sort(np.concatenate(ns)), np.sort(near))
+        assert np.array_equal(np.concatenate(fs), far)
+
+
+def _gloo_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from foveated_kv_b200.seqsplit import shard_bounds, gather_partials
+    S, cfg = 600, dict(near_pct=0.1, window_size=16)
+    w = numpy_workload(5, 1, 2, 8, S, 64, 0)
+    lo, hi = shard_bounds(S, rank, world)
+    lay, off = _oracle_shard(w, S, lo, hi, cfg)
+    m, l, o, mn, mf, arg = O.decode_partials(lay, w["q"], far_offset=off)
+    part = torch.from_numpy(np.concatenate([np.stack([m, l, mn, mf], 1), o], 1))
+    parts, args = gather_partials(part, torch.from_numpy(arg.astype(np.int32)))
+    if rank == 0:
+        P = parts.numpy()
+        out, fl, tk = O.combine_partials(P[:, :, 0], P[:, :, 1], P[:, :, 4:], P[:, :, 2],
+                                         P[:, :, 3], args.numpy(), 0.5)
+        full = O.compress_layer(w["k"], w["v"], cfg)
+        rout, rfl, rtk, _ = O.decode_attend(full, w["q"], None, None, 0.5)
+        q.put((float(np.abs(out - rout.reshape(out.shape)).max()),
+               bool(np.array_equal(fl, rfl.reshape(-1))), bool(np.array_equal(tk, rtk.reshape(-1)))))
+    dist.destroy_process_group()
+
+
+def test_gloo_two_rank_exchange_matches_unsplit():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_gloo_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    err, fl_ok, tk_ok = q.get(timeout=120)
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert err < 1e-9 and fl_ok and tk_ok
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("P", [1, 2, 3, 8])
+def test_partials_on_one_gpu_equal_unsplit(P):
+    from foveated_kv_b200 import TierConfig, compress_layer
+    from foveated_kv_b200.seqsplit import shard_bounds, compress_shard, decode_partial, combine
+    S, B, Hk, Hq, D = 4000, 2, 2, 8, 128
+    w = numpy_workload(9, B, Hk, Hq, S, D, 0)
+    t = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
+    cfg = TierConfig(near_pct=0.05, window_size=32, spike_margin=0.5)
+    full = compress_layer(t["k"], t["v"], cfg)
+    ref_out, ref_fl, ref_tk = full.attend_fused_with_spikes(t["q"])
+    parts, args = [], []
+    for r in range(P):
+        lo, hi = shard_bounds(S, r, P)
+        lay, off = compress_shard(t["k"][:, :, lo:hi], t["v"][:, :, lo:hi], S, lo, cfg)
+        pa, ar = decode_partial(lay, t["q"], off)
+        parts.append(pa); args.append(ar)
+    out, fl, tk = combine(torch.stack(parts), torch.stack(args), 0.5)
+    torch.cuda.synchronize()
+    assert (out.float() - ref_out.float().reshape(out.shape)).abs().max().item() < 2e-3
+    assert torch.equal(fl.cpu(), ref_fl.reshape(-1).cpu())
+    assert torch.equal(tk.cpu(), ref_tk.reshape(-1).cpu())
+    rout, rfl, rtk, _ = O.decode_attend(
+        O.compress_layer(w["k"], w["v"], dict(near_pct=0.05, window_size=32)), w["q"], None, None, 0.5)
+    assert np.abs(out.float().cpu().numpy() - rout.reshape(B * Hq, D)).max() < 2e-3
+
+
+@pytest.mark.gpu
+def test_nccl_seqsplit_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node=2", "--master-addr=127.0.0.1",
+                        f"--master-port={_free_port()}", os.path.join(ROOT, "tests", "seqsplit_worker.py")],
+                       capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert "SEQSPLIT_OK" in r.stdout
