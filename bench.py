@@ -36,7 +36,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 N_LAYERS = 32          # tokens/s = B / (32 x t_layer), attention only
-METRIC = "decode attention tokens/s (B / (32 layers x per-layer fused decode time)), 1-layer c3"
+METRIC_FMT = "decode attention tokens/s (B / (32 layers x per-layer fused decode time)), 1-layer {}"
+METRIC = METRIC_FMT.format("c3")
 
 
 def parse():
@@ -45,7 +46,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c3", choices=["c3", "c1_16k", "c1_8k", "c1_4k", "c1_1k", "c0"])
+    ap.add_argument("--config", default="c3",
+                    choices=["c3", "c1_16k", "c1_8k", "c1_4k", "c1_1k", "c0", "c2", "c4"])
     ap.add_argument("--cpu-sample-seqs", type=int, default=1)
     ap.add_argument("--batch", type=int, default=0, help="override sequences per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -157,7 +159,7 @@ class CpuArm:
         self.w = numpy_workload(7, self.seqs, c["Hk"], c["Hq"], c["S"], c["D"], c["n_dec"])
         self.lay = O.compress_layer(self.w["k"], self.w["v"], dict(
             near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
-            v_group=c["v_group"]))
+            v_group=c["v_group"], compress_method=c["compress_method"]))
 
     def run(self):
         t0 = time.perf_counter()
@@ -190,7 +192,7 @@ def reference_arm(args, rank, world):
     dts = [arm.run() for _ in range(args.steps)]
     el = time.perf_counter() - t0
     d = arm.describe(statistics.median(dts))
-    line = {"impl": "reference", "metric": METRIC, "value": d["value"], "unit": "tokens/s",
+    line = {"impl": "reference", "metric": METRIC_FMT.format(args.config), "value": d["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -201,6 +203,107 @@ def reference_arm(args, rank, world):
             "note": "reference CPU path = NumPy restatement of mlx_foveated.attend "
                     "(MLX/Metal cannot run on Linux/B200)"}
     print(json.dumps(line), flush=True)
+
+
+def main_seqsplit(args, rank, world, device):
+    """c4: one 1M-token sequence split evenly over the ranks; per step each
+    rank decodes its shard in partial mode, the (m, l, o) records are
+    all-gathered over NCCL and merged (strong scaling).  Also times the
+    compression pass of each rank's freshly prefilled shard."""
+    import torch
+    import torch.distributed as dist
+    from foveated_kv_b200 import TierConfig
+    from foveated_kv_b200.seqsplit import shard_bounds, compress_shard, decode_seqsplit
+    from foveated_kv_b200.synthetic import torch_workload, CONFIGS
+    c = CONFIGS["c4"]
+    B, Hq, Hk, D, S = c["B"], c["Hq"], c["Hk"], c["D"], c["S"]
+    cfg = TierConfig(near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
+                     spike_margin=0.5)
+    lo, hi = shard_bounds(S, rank, world)
+    w = torch_workload(4000 + rank, B, Hk, Hq, hi - lo, D, 0, device)
+    g = torch.Generator(device=device)
+    g.manual_seed(77)
+    q = torch.randn((B, Hq, D), generator=g, device=device, dtype=torch.float16)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    compress_shard(w["k"][:, :, :4096], w["v"][:, :, :4096], S, lo, cfg)   # warm-up
+    torch.cuda.synchronize()
+    e0.record()
+    lay, off = compress_shard(w["k"], w["v"], S, lo, cfg)
+    e1.record()
+    torch.cuda.synchronize()
+    compress_ms = e0.elapsed_time(e1)
+    del w
+    for _ in range(max(args.warmup, 3)):
+        decode_seqsplit(lay, q, off)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) as clk:
+        e0.record()
+        for _ in range(args.steps):
+            decode_seqsplit(lay, q, off)
+        e1.record()
+        torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    nv_sum = int(lay.near_valid.sum().item())
+    alg_local = algorithmic_bytes(B, Hq, Hk, D, nv_sum, lay.n_far, 0)
+    t = torch.tensor([ms, compress_ms, float(alg_local)], device=device, dtype=torch.float64)
+    if world > 1:
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = t.clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        ms, compress_ms, alg_total = float(mx[0]), float(mx[1]), float(tot[2])
+    else:
+        alg_total = float(alg_local)
+    q_host = q.cpu().pin_memory()
+    q_dev = torch.empty_like(q)
+    outs_h = [torch.empty((B, Hq, 1, D), dtype=torch.float16).pin_memory(),
+              torch.empty((B, Hq), dtype=torch.int32).pin_memory(),
+              torch.empty((B, Hq), dtype=torch.int32).pin_memory()]
+    st = torch.cuda.current_stream()
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        for h, d in zip(outs_h, decode_seqsplit(lay, q_dev, off)):
+            h.copy_(d, non_blocking=True)
+        st.synchronize()
+
+    for _ in range(3):
+        e2e_step()
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms_e2e = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms_e2e], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_e2e = float(t.item())
+    peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"] \
+        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 6650.0
+    achieved = alg_total / world / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC_FMT.format("c4"), "value": B / (N_LAYERS * ms * 1e-3),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,1) fp16)",
+            "config": {"workload": "c4", "B": B, "Hq": Hq, "Hk": Hk, "D": D, "S": S,
+                       "near_pct": c["near_pct"], "parallelism": f"sequence split x{world}",
+                       "exchange": "NCCL all-gather of (m, l, o) records + combine kernel"},
+            "us_per_layer": ms * 1e3, "compress_ms": compress_ms,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "algorithmic_bytes_per_launch": alg_total / world,
+                         "traffic": None, "note": "per-GPU bytes / step time (includes all-gather)"},
+            "e2e": {"value": B / (N_LAYERS * ms_e2e * 1e-3), "unit": "tokens/s",
+                    "ms_per_step": ms_e2e, "h2d_bytes_per_step": q.numel() * 2,
+                    "d2h_bytes_per_step": B * Hq * (2 * D + 8)},
+            "gpu_launches": args.steps * 2, "clocks": clk.summary(), "cpu_baseline": None}),
+            flush=True)
+    dist.destroy_process_group() if world > 1 else None
 
 
 def main():
@@ -218,11 +321,12 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", device_id=device)
     from foveated_kv_b200 import _native  # noqa: F401
+    if args.config == "c4":
+        return main_seqsplit(args, rank, world, device)
 
     c, cfg, lay, q = build_layer(args.config, 1000 + rank, device, args.batch)
     B, Hq, Hk, D = c["B"], c["Hq"], c["Hk"], c["D"]
-    tier_bytes = sum(t.numel() * t.element_size() for t in (
-        lay.near_k, lay.near_v, lay.far_k, lay.far_v, lay.far_v_scale, lay.far_v_zero))
+    tier_bytes = lay.memory_bytes()["total_quantized"]
     # distinct layers so that one graph replay streams >= ~4 GB (no L2 reuse
     # across layers); c0 fits in L2 whatever we do and is reported as latency
     n_layers = max(1, min(N_LAYERS, int(4e9 // max(tier_bytes, 1))))
@@ -316,13 +420,16 @@ def main():
     achieved = alg / (ms * 1e-3) / 1e9
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "metric": METRIC_FMT.format(args.config), "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (seeded N(0,1) fp16, 4 outlier K channels/head, 1% spikes)",
             "config": {"workload": args.config, "B_per_gpu": B, "Hq": Hq, "Hk": Hk, "D": D,
                        "S": c["S"], "near_pct": c["near_pct"], "window": c["window_size"],
-                       "far_tier": "fp8 E4M3 K + per-token INT4 V",
+                       "far_tier": ("TurboQuant 2-bit K + 1-bit QJL, 2-bit V/32" if
+                                    cfg.compress_method == "turbo" else
+                                    "fp8 E4M3 K + INT4 V (" + ("per token" if c["v_group"] is None
+                                                              else "group 32") + ")"),
                        "global_batch": B * world, "parallelism": f"batch-shard x{world}",
                        "l2": "inputs larger than L2 (no flush)"},
             "us_per_layer": ms * 1e3, "hbm_gbs": achieved,
