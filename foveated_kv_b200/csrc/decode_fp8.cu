@@ -400,11 +400,14 @@ __global__ void turbo_qproj_kernel(const uint16_t* __restrict__ q, const float* 
     for (int i = threadIdx.x; i < D; i += blockDim.x)
         qv[i] = __half2float(__ushort_as_half(q[(int64_t)bh * D + i]));
     __syncthreads();
-    for (int o = threadIdx.x; o < 2 * D; o += blockDim.x) {
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int o = w; o < 2 * D; o += nw) {   // one warp per output, lanes along the row
         const float* row = (o < D ? Pi + (int64_t)o * D : Sm + (int64_t)(o - D) * D);
         float acc = 0.f;
-        for (int i = 0; i < D; ++i) acc = fmaf(qv[i], __ldg(row + i), acc);
-        out[(int64_t)bh * 2 * D + o] = acc;
+#pragma unroll
+        for (int i = lane; i < D; i += 32) acc = fmaf(qv[i], __ldg(row + i), acc);
+        for (int x = 16; x > 0; x >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, x);
+        if (lane == 0) out[(int64_t)bh * 2 * D + o] = acc;
     }
 }
 
@@ -575,64 +578,87 @@ __device__ __forceinline__ void turbo_tile(const DecodeParams& p, const uint8_t*
     }
 }
 
-// merge `n` records (strided by `stride` floats) into the caller's registers:
-// each thread handles (head, d) pairs e = tid, tid+nthreads, ...
+// Merge `n` records (strided by `stride` floats; in shared memory for the
+// per-warp records, in the workspace for split records) and emit the output
+// or the sequence-split record.  The records' scalars are first staged in
+// shared memory with independent loads, per-head maxima / weights computed
+// once, then every thread accumulates its (head, d) outputs over the records
+// with many independent, coalesced loads in flight.
+constexpr int kMaxSplits = 64;
+
 template <int D>
 __device__ __forceinline__ void merge_and_emit(const DecodeParams& p, const float* recs, int n,
-                                               int stride, int s, int hg, bool from_global) {
+                                               int stride, int s, int hg, bool from_global,
+                                               float* __restrict__ scratch) {
     using R = RecLayout<D>;
     const int tid = threadIdx.x;
     const int b = s / p.Hk, h = s % p.Hk;
-    auto ld = [&](const float* a) { return from_global ? __ldcg(a) : *a; };
-    for (int e = tid; e < kHeadsPerTile * D; e += kConsumerThreads) {
-        const int head = e / D, d = e % D;
+    float* sc = scratch;                      // [n][40] record scalars
+    float* wk = scratch + kMaxSplits * 40;    // [n][8] weights exp(m_k - M)
+    float* hl = wk + kMaxSplits * 8;          // [8] L per head
+    for (int i = tid; i < n * 40; i += kConsumerThreads) {
+        const float* a = recs + (i / 40) * stride + (i % 40);
+        sc[i] = from_global ? __ldcg(a) : *a;
+    }
+    named_sync(1, kConsumerThreads);
+    if (tid < 8) {
+        const int head = tid;
         const int g = hg * kHeadsPerTile + head;
-        if (g >= p.G) continue;
         float M = -INFINITY;
-        for (int k = 0; k < n; ++k) M = fmaxf(M, ld(recs + k * stride + R::M + head));
-        float L = 0.f, acc = 0.f;
-        if (M != -INFINITY) {
-            for (int k = 0; k < n; ++k) {
-                const float mk = ld(recs + k * stride + R::M + head);
-                if (mk == -INFINITY) continue;
-                const float w = exp2f((mk - M) * kLog2e);
-                L = fmaf(w, ld(recs + k * stride + R::L + head), L);
-                acc = fmaf(w, ld(recs + k * stride + R::O + head * D + d), acc);
-            }
+        for (int k = 0; k < n; ++k) M = fmaxf(M, sc[k * 40 + R::M + head]);
+        float L = 0.f, mn = INFINITY, mf = -INFINITY;
+        int af = -1;
+        for (int k = 0; k < n; ++k) {
+            const float mk = sc[k * 40 + R::M + head];
+            const float wgt = (mk == -INFINITY) ? 0.f : exp2f((mk - M) * kLog2e);
+            wk[k * 8 + head] = wgt;
+            L = fmaf(wgt, sc[k * 40 + R::L + head], L);
+            mn = fminf(mn, sc[k * 40 + R::MN + head]);
+            argmax_merge(mf, af, sc[k * 40 + R::MF + head], __float_as_int(sc[k * 40 + R::AF + head]));
         }
-        const int64_t bh = (int64_t)b * p.Hq + (int64_t)h * p.G + g;
-        if (p.part != nullptr) {
-            float* rec = p.part + bh * (D + 4);
-            rec[4 + d] = acc;
-            if (d == 0) {
-                float mn = INFINITY, mf = -INFINITY;
-                int af = -1;
-                for (int k = 0; k < n; ++k) {
-                    mn = fminf(mn, ld(recs + k * stride + R::MN + head));
-                    const float f = ld(recs + k * stride + R::MF + head);
-                    const float ai = ld(recs + k * stride + R::AF + head);
-                    argmax_merge(mf, af, f, __float_as_int(ai));
-                }
+        hl[head] = L;
+        if (g < p.G) {
+            const int64_t bh = (int64_t)b * p.Hq + (int64_t)h * p.G + g;
+            if (p.part != nullptr) {
+                float* rec = p.part + bh * (D + 4);
                 rec[0] = M;
                 rec[1] = L;
                 rec[2] = mn;
                 rec[3] = mf;
                 p.part_arg[bh] = af >= 0 ? af + p.far_offset : -1;
-            }
-        } else {
-            p.out[bh * D + d] = __half_as_ushort(__float2half_rn(L > 0.f ? acc / L : 0.f));
-            if (d == 0) {
-                float mn = INFINITY, mf = -INFINITY;
-                int af = -1;
-                for (int k = 0; k < n; ++k) {
-                    mn = fminf(mn, ld(recs + k * stride + R::MN + head));
-                    const float f = ld(recs + k * stride + R::MF + head);
-                    const float ai = ld(recs + k * stride + R::AF + head);
-                    argmax_merge(mf, af, f, __float_as_int(ai));
-                }
+            } else {
                 p.flags[bh] = (mf > mn + p.margin) ? 1 : 0;
                 p.tokens[bh] = af;
             }
+        }
+    }
+    named_sync(1, kConsumerThreads);
+    constexpr int E = kHeadsPerTile * D / kConsumerThreads;   // outputs per thread
+    float acc[E];
+#pragma unroll
+    for (int x = 0; x < E; ++x) acc[x] = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < n; ++k) {
+        const float* o = recs + k * stride + R::O;
+#pragma unroll
+        for (int x = 0; x < E; ++x) {
+            const int e = tid + x * kConsumerThreads;
+            const float v = from_global ? __ldcg(o + e) : o[e];
+            acc[x] = fmaf(wk[k * 8 + e / D], v, acc[x]);
+        }
+    }
+#pragma unroll
+    for (int x = 0; x < E; ++x) {
+        const int e = tid + x * kConsumerThreads;
+        const int head = e / D, d = e % D;
+        const int g = hg * kHeadsPerTile + head;
+        if (g >= p.G) continue;
+        const int64_t bh = (int64_t)b * p.Hq + (int64_t)h * p.G + g;
+        if (p.part != nullptr) {
+            p.part[bh * (D + 4) + 4 + d] = acc[x];
+        } else {
+            const float L = hl[head];
+            p.out[bh * D + d] = __half_as_ushort(__float2half_rn(L > 0.f ? acc[x] / L : 0.f));
         }
     }
 }
@@ -834,7 +860,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
     named_sync(1, kConsumerThreads);
 
     if (p.splits == 1) {
-        merge_and_emit<D>(p, sh_rec, kConsumerWarps, R::SIZE, s, hg, false);
+        merge_and_emit<D>(p, sh_rec, kConsumerWarps, R::SIZE, s, hg, false,
+                          sh_rec + kConsumerWarps * R::SIZE);
         return;
     }
 
@@ -890,7 +917,7 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
     if (!sh_last) return;
     __threadfence();
     const float* base = p.ws + ((int64_t)s * p.HG + hg) * p.splits * R::SIZE;
-    merge_and_emit<D>(p, base, p.splits, R::SIZE, s, hg, true);
+    merge_and_emit<D>(p, base, p.splits, R::SIZE, s, hg, true, sh_rec);
 }
 
 template <int D>
@@ -976,6 +1003,7 @@ Plan make_plan(const FkvDecodeShape* sh) {
             }
         }
     }
+    splits = std::min(splits, kMaxSplits);
     int64_t chunk = (T + splits - 1) / splits;
     constexpr int64_t q = 64;   // chunk granularity (tokens)
     chunk = std::max<int64_t>(q, (chunk + q - 1) / q * q);

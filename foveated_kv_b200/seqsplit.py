@@ -107,6 +107,8 @@ def decode_partial(layer: FoveatedLayer, q: torch.Tensor, far_offset: int):
 def gather_partials(part: torch.Tensor, arg: torch.Tensor, group=None):
     """All-gather every rank's records: (P, N, D+4) and (P, N), rank order.
     NCCL over NVLink on GPUs; any backend works (gloo for host tests)."""
+    if not (dist.is_available() and dist.is_initialized()):
+        return part[None], arg[None]          # single process: nothing to exchange
     P = dist.get_world_size(group)
     parts = torch.empty((P * part.shape[0],) + tuple(part.shape[1:]), dtype=part.dtype,
                         device=part.device)
