@@ -127,12 +127,38 @@ struct Ring {
     static constexpr int NEAR_TOK = 64;
     static constexpr int VOFF = NEAR_TOK * D * 2;        // K region (max of near / far)
     static constexpr int SLOT = VOFF + NEAR_TOK * D * 2;  // + V region
+    // per-token scalars of a far stage (INT4 scale / zero, or turbo norm /
+    // gamma / value scales / QJL signs), each a 16-byte-aligned covering copy
+    static constexpr int SEL = (VG == 0) ? 1 : D / 32;           // halves per token in r0/r1
+    static constexpr int SZOFF = VOFF + FAR_TOK * (VG == kTurbo ? D / 4 : D / 2);
+    static constexpr int RB0 = FAR_TOK * SEL * 2 + 32;           // region bytes (r0, r1)
+    static constexpr int RB2 = FAR_TOK * (D / 32) * 2 + 32;      // turbo value scales
+    static constexpr int RB3 = FAR_TOK * (D / 8) + 32;           // turbo signs
+    static_assert(SZOFF + 2 * RB0 + (VG == kTurbo ? RB2 + RB3 : 0) <= SLOT, "slot overflow");
     static constexpr int QFRAG = (D / 16) * 32 * 16;            // one set of q fragments
     static constexpr int QOFF = kStages * SLOT;                 // q (+ turbo q Pi^T, q S^T)
     static constexpr int TSUM = QOFF + (VG == kTurbo ? 3 : 1) * QFRAG;   // turbo row sums
     static constexpr int BAROFF = TSUM + (VG == kTurbo ? 64 : 0);        // mbarriers
     static constexpr int BYTES = BAROFF + 2 * kStages * 8;
 };
+
+// Bytes [b0, b1) of `base` (an array of `total` bytes) into shared `dst`,
+// which receives the 16-byte-aligned covering range starting at b0 & ~15: a
+// bulk copy for the part inside the array's last full 16 bytes, plain loads
+// for a ragged end of the array.  Returns the bulk bytes (for expect_tx).
+__device__ __forceinline__ uint32_t copy_covering(uint8_t* dst, const uint8_t* base, int64_t total,
+                                                  int64_t b0, int64_t b1, uint64_t* bar) {
+    const int64_t a0 = b0 & ~(int64_t)15;
+    const int64_t a1 = (b1 + 15) & ~(int64_t)15;
+    const int64_t bulk_end = min(a1, total & ~(int64_t)15);
+    uint32_t tx = 0;
+    if (bulk_end > a0) {
+        bulk_g2s(dst, base + a0, (uint32_t)(bulk_end - a0), bar);
+        tx = (uint32_t)(bulk_end - a0);
+    }
+    for (int64_t x = max(a0, bulk_end); x < b1; ++x) dst[x - a0] = base[x];
+    return tx;
+}
 
 struct Segs {
     int a[3], e[3], n[3];   // tier-local [a, e) and stage counts: near, far, decode
@@ -221,27 +247,16 @@ __device__ __forceinline__ void fp16_tile(const uint8_t* __restrict__ kbuf,
 // scale/zero of the 4 V tokens a lane feeds into the PV product, packed
 // (scale | zero << 16); loaded one stage ahead from global memory
 template <int D, int VG>
-__device__ __forceinline__ void load_sz(const DecodeParams& p, int64_t srow0, int start, int u0,
-                                        int cnt, int lane, uint32_t (&sz)[4]) {
+__device__ __forceinline__ void load_sz(const uint16_t* __restrict__ sc,
+                                        const uint16_t* __restrict__ ze, int u0, int cnt,
+                                        int lane, uint32_t (&sz)[4]) {
     const int r = lane >> 2, c = lane & 3;
+    constexpr int EL = (VG == 0) ? 1 : D / VG;   // values per token
+    const int grp = (VG == 0) ? 0 : (r * (D / 8)) / (VG == 0 ? 1 : VG);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         const int u = u0 + (e >> 1) * 8 + 2 * c + (e & 1);
-        if (u < cnt) {
-            const int64_t row = srow0 + start + u;
-            uint16_t sv, zv;
-            if constexpr (VG == 0) {
-                sv = __ldg(p.v_scale + row);
-                zv = __ldg(p.v_zero + row);
-            } else {
-                const int grp = (r * (D / 8)) / VG;
-                sv = __ldg(p.v_scale + row * (D / VG) + grp);
-                zv = __ldg(p.v_zero + row * (D / VG) + grp);
-            }
-            sz[e] = (uint32_t)sv | ((uint32_t)zv << 16);
-        } else {
-            sz[e] = 0u;
-        }
+        sz[e] = u < cnt ? ((uint32_t)sc[u * EL + grp] | ((uint32_t)ze[u * EL + grp] << 16)) : 0u;
     }
 }
 
@@ -450,23 +465,19 @@ __device__ __forceinline__ void build_turbo_frags(const DecodeParams& p, int s, 
 
 // norm | gamma << 16 and the value group scale of the lane's 4 PV tokens
 template <int D>
-__device__ __forceinline__ void load_turbo_sz(const DecodeParams& p, int64_t srow0, int start,
-                                              int u0, int cnt, int lane, uint32_t (&ng)[4],
-                                              uint32_t (&vs)[2]) {
+__device__ __forceinline__ void load_turbo_sz(const uint16_t* __restrict__ nm,
+                                              const uint16_t* __restrict__ gm,
+                                              const uint16_t* __restrict__ vsc, int u0, int cnt,
+                                              int lane, uint32_t (&ng)[4], uint32_t (&vs)[2]) {
     const int r = lane >> 2, c = lane & 3;
     const int grp = (r * (D / 8)) / 32;
     uint16_t sv[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         const int u = u0 + (e >> 1) * 8 + 2 * c + (e & 1);
-        if (u < cnt) {
-            const int64_t row = srow0 + start + u;
-            ng[e] = (uint32_t)__ldg(p.k_norm + row) | ((uint32_t)__ldg(p.k_gamma + row) << 16);
-            sv[e] = __ldg(p.v_scale + row * (D / 32) + grp);
-        } else {
-            ng[e] = 0u;
-            sv[e] = 0;
-        }
+        const bool ok = u < cnt;
+        ng[e] = ok ? ((uint32_t)nm[u] | ((uint32_t)gm[u] << 16)) : 0u;
+        sv[e] = ok ? vsc[u * (D / 32) + grp] : (uint16_t)0;
     }
     vs[0] = (uint32_t)sv[0] | ((uint32_t)sv[1] << 16);
     vs[1] = (uint32_t)sv[2] | ((uint32_t)sv[3] << 16);
@@ -476,7 +487,8 @@ __device__ __forceinline__ void load_turbo_sz(const DecodeParams& p, int64_t sro
 __device__ __forceinline__ uint32_t bits2_to_h2(uint32_t x) { return (x & 0x00010001u) * 0x3C00u; }
 
 template <int D>
-__device__ __forceinline__ void turbo_tile(const DecodeParams& p, const uint8_t* __restrict__ kbuf,
+__device__ __forceinline__ void turbo_tile(const uint8_t* __restrict__ sgn,
+                                           const uint8_t* __restrict__ kbuf,
                                            const uint8_t* __restrict__ vbuf, int u0, int cnt,
                                            int64_t srow0, int gbase, int lane,
                                            const uint4* __restrict__ qr,
@@ -497,10 +509,9 @@ __device__ __forceinline__ void turbo_tile(const DecodeParams& p, const uint8_t*
             const uint4 w4 = src[x];
             kr[n][4 * x] = w4.x; kr[n][4 * x + 1] = w4.y; kr[n][4 * x + 2] = w4.z; kr[n][4 * x + 3] = w4.w;
         }
-        const bool ok = u < cnt;
-        const uint32_t* gs = reinterpret_cast<const uint32_t*>(p.k_signs + (srow0 + gbase + u) * SB);
+        const uint8_t* gs = sgn + u * SB;   // may be only 8-byte aligned (D = 64)
 #pragma unroll
-        for (int x = 0; x < SB / 4; ++x) sg[n][x] = ok ? __ldg(gs + x) : 0u;
+        for (int x = 0; x < SB / 4; ++x) sg[n][x] = *reinterpret_cast<const uint32_t*>(gs + 4 * x);
     }
     float acc[4][2][4];
 #pragma unroll
@@ -731,9 +742,31 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
                     vs = (seg == 0 ? nvp : dv) + (int64_t)start * D * 2;
                     kb = vb = cnt * D * 2;
                 }
-                mbar_arrive_expect_tx(full + slot, kb + vb);
                 bulk_g2s(dst, ks, kb, full + slot);
                 bulk_g2s(dst + RG::VOFF, vs, vb, full + slot);
+                uint32_t tx = kb + vb;
+                if (seg == 1) {
+                    const int64_t row0 = (int64_t)s * p.F + start, nrows = (int64_t)p.B * p.Hk * p.F;
+                    uint8_t* sd = dst + RG::SZOFF;
+                    if constexpr (VG == kTurbo) {
+                        const int64_t vsb = 2 * (D / 32);
+                        tx += copy_covering(sd, (const uint8_t*)p.k_norm, nrows * 2, row0 * 2,
+                                            (row0 + cnt) * 2, full + slot);
+                        tx += copy_covering(sd + RG::RB0, (const uint8_t*)p.k_gamma, nrows * 2,
+                                            row0 * 2, (row0 + cnt) * 2, full + slot);
+                        tx += copy_covering(sd + 2 * RG::RB0, (const uint8_t*)p.v_scale, nrows * vsb,
+                                            row0 * vsb, (row0 + cnt) * vsb, full + slot);
+                        tx += copy_covering(sd + 2 * RG::RB0 + RG::RB2, p.k_signs, nrows * (D / 8),
+                                            row0 * (D / 8), (row0 + cnt) * (D / 8), full + slot);
+                    } else {
+                        const int64_t eb = 2 * RG::SEL;
+                        tx += copy_covering(sd, (const uint8_t*)p.v_scale, nrows * eb, row0 * eb,
+                                            (row0 + cnt) * eb, full + slot);
+                        tx += copy_covering(sd + RG::RB0, (const uint8_t*)p.v_zero, nrows * eb,
+                                            row0 * eb, (row0 + cnt) * eb, full + slot);
+                    }
+                }
+                mbar_arrive_expect_tx(full + slot, tx);
             }
         }
         return;
@@ -762,28 +795,11 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
     WarpState<D> st;
     st.init();
     const int64_t srow0 = (int64_t)s * p.F;
-    uint32_t szc[2][4], szn[2][4];
-    uint32_t vsc[2][2], vsn[2][2];   // turbo: value group scales
-    auto prefetch = [&](int k, uint32_t (&dst)[2][4], uint32_t (&vdst)[2][2]) {
-        if (k >= nstage) return;
-        int seg, start, cnt;
-        stage_at<D>(sg, k, seg, start, cnt);
-        if (seg != 1) return;
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-            if constexpr (VG == kTurbo)
-                load_turbo_sz<D>(p, srow0, start, (w + 4 * x) * kTile, cnt, lane, dst[x], vdst[x]);
-            else
-                load_sz<D, VG>(p, srow0, start, (w + 4 * x) * kTile, cnt, lane, dst[x]);
-        }
-    };
-    prefetch(0, szc, vsc);
     int failed_at = -1;
     for (int k = 0; k < nstage; ++k) {
         const int slot = k % kStages;
         int seg, start, cnt;
         stage_at<D>(sg, k, seg, start, cnt);
-        prefetch(k + 1, szn, vsn);
         if (!mbar_wait(full + slot, (k / kStages) & 1)) {
             atomicExch(p.status, FKV_ERR_TIMEOUT);
             failed_at = k;
@@ -792,37 +808,48 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
         const uint8_t* kbuf = smem + slot * RG::SLOT;
         const uint8_t* vbuf = kbuf + RG::VOFF;
         const int ntile = (cnt + kTile - 1) / kTile;
-        if (seg == 1 && VG == kTurbo) {
+        if (seg == 1) {
+            // stage scalars: covering copies start at the 16-byte boundary below
+            const int64_t row0 = srow0 + start;
+            const uint8_t* sd = kbuf + RG::SZOFF;
+            if constexpr (VG == kTurbo) {
+                const uint16_t* nm = reinterpret_cast<const uint16_t*>(sd + ((row0 * 2) & 15));
+                const uint16_t* gm = reinterpret_cast<const uint16_t*>(sd + RG::RB0 + ((row0 * 2) & 15));
+                const uint16_t* vsp = reinterpret_cast<const uint16_t*>(
+                    sd + 2 * RG::RB0 + ((row0 * 2 * (D / 32)) & 15));
+                const uint8_t* sgn = sd + 2 * RG::RB0 + RG::RB2 + ((row0 * (D / 8)) & 15);
 #pragma unroll
-            for (int x = 0; x < 2; ++x) {
-                const int i = w + 4 * x;
-                if (i < ntile)
-                    turbo_tile<D>(p, kbuf, vbuf, i * kTile, cnt, srow0, start, lane, qr, qk, cf,
-                                  sum_r, sum_k, szc[x], vsc[x], st);
+                for (int x = 0; x < 2; ++x) {
+                    const int i = w + 4 * x;
+                    if (i < ntile) {
+                        uint32_t ng[4], vs2[2];
+                        load_turbo_sz<D>(nm, gm, vsp, i * kTile, cnt, lane, ng, vs2);
+                        turbo_tile<D>(sgn, kbuf, vbuf, i * kTile, cnt, srow0, start, lane, qr, qk,
+                                      cf, sum_r, sum_k, ng, vs2, st);
+                    }
+                }
+            } else {
+                constexpr int eb = 2 * RG::SEL;
+                const uint16_t* sc = reinterpret_cast<const uint16_t*>(sd + ((row0 * eb) & 15));
+                const uint16_t* ze = reinterpret_cast<const uint16_t*>(sd + RG::RB0 + ((row0 * eb) & 15));
+                if (w + 4 < ntile) {
+                    const int u0[2] = {w * kTile, (w + 4) * kTile};
+                    uint32_t sz[2][4];
+                    load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
+                    load_sz<D, VG>(sc, ze, u0[1], cnt, lane, sz[1]);
+                    far_tiles<D, VG, 2>(kbuf, vbuf, u0, cnt, start, lane, qs, sz, st);
+                } else if (w < ntile) {
+                    const int u0[1] = {w * kTile};
+                    uint32_t sz[1][4];
+                    load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
+                    far_tiles<D, VG, 1>(kbuf, vbuf, u0, cnt, start, lane, qs, sz, st);
+                }
             }
-        } else if (seg == 1) {
-          if constexpr (VG != kTurbo) {
-            if (w + 4 < ntile) {
-                const int u0[2] = {w * kTile, (w + 4) * kTile};
-                far_tiles<D, VG, 2>(kbuf, vbuf, u0, cnt, start, lane, qs, szc, st);
-            } else if (w < ntile) {
-                const int u0[1] = {w * kTile};
-                const uint32_t (&sz1)[1][4] = *reinterpret_cast<const uint32_t (*)[1][4]>(&szc[0]);
-                far_tiles<D, VG, 1>(kbuf, vbuf, u0, cnt, start, lane, qs, sz1, st);
-            }
-          }
         } else if (w < ntile) {
             fp16_tile<D>(kbuf, vbuf, w * kTile, cnt, lane, qs, st);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + slot);
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e) szc[x][e] = szn[x][e];
-            vsc[x][0] = vsn[x][0];
-            vsc[x][1] = vsn[x][1];
-        }
     }
     if (failed_at >= 0) {
         // the producer runs at most kStages ahead of the consumers: wait
@@ -1089,10 +1116,10 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     }
     if (sh->D == 128) {
         if (sh->v_group == 0) return launch_kernel(decode_fp8_kernel<128, 0>, Ring<128>::BYTES, grid, p, st);
-        return launch_kernel(decode_fp8_kernel<128, 32>, Ring<128>::BYTES, grid, p, st);
+        return launch_kernel(decode_fp8_kernel<128, 32>, Ring<128, 32>::BYTES, grid, p, st);
     }
     if (sh->v_group == 0) return launch_kernel(decode_fp8_kernel<64, 0>, Ring<64>::BYTES, grid, p, st);
-    return launch_kernel(decode_fp8_kernel<64, 32>, Ring<64>::BYTES, grid, p, st);
+    return launch_kernel(decode_fp8_kernel<64, 32>, Ring<64, 32>::BYTES, grid, p, st);
 }
 
 int fill_common(const FkvDecodeShape* sh, DecodeParams& p, const uint16_t* near_k,

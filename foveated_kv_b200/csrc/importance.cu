@@ -103,7 +103,7 @@ __global__ void __launch_bounds__(kSelThreads)
     __shared__ typename Scan::TempStorage scan_tmp;
     __shared__ unsigned int hist[256];
     __shared__ uint64_t sh_prefix;
-    __shared__ int sh_krem, sh_digit;
+    __shared__ int sh_krem;
     __shared__ int sh_run[3];
     const int s = blockIdx.x, tid = threadIdx.x;
     const int Np = L.n_near_padded, F = L.far_count;
@@ -132,7 +132,6 @@ __global__ void __launch_bounds__(kSelThreads)
                     if (acc + (int)hist[d] >= krem) break;
                     acc += hist[d];
                 }
-                sh_digit = d;
                 sh_krem = krem - acc;
                 sh_prefix = prefix | ((uint64_t)d << shift);
             }
