@@ -418,6 +418,11 @@ def main():
     else:
         peak, peak_src = 6650.0, "fallback"
     achieved = alg / (ms * 1e-3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath) and not args.batch:
+        with open(tpath) as f:
+            traffic = json.load(f).get(args.config, {}).get("traffic_bytes_per_launch")
     if rank == 0:
         line = {
             "metric": METRIC_FMT.format(args.config), "value": value, "unit": "tokens/s", "n_gpus": world,
@@ -435,7 +440,8 @@ def main():
             "us_per_layer": ms * 1e3, "hbm_gbs": achieved,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_src,
-                         "algorithmic_bytes_per_launch": alg, "traffic": None},
+                         "algorithmic_bytes_per_launch": alg, "traffic": traffic,
+                         "traffic_source": "ncu dram__bytes_read+write per launch (profiles/)"},
             "e2e": {"value": world * B / (N_LAYERS * ms_e2e * 1e-3), "unit": "tokens/s",
                     "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps * n_layers,

@@ -694,8 +694,16 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
         fence_mbar_init();
     }
     // segments of this split's chunk [t0, t1) of [near valid | far | decode]
-    const int t0 = split * p.chunk;
-    const int t1 = min(t0 + p.chunk, p.Np + p.F + p.n_dec);
+    // splits are even in cost units (an fp16 near / decode token weighs 2, a
+    // compressed far token 1); map this split's cost range back to tokens
+    auto to_tok = [&](int64_t cu) -> int {
+        if (cu <= 2 * (int64_t)p.Np) return (int)(cu / 2);
+        if (cu <= 2 * (int64_t)p.Np + p.F) return (int)(cu - p.Np);
+        return p.Np + p.F + (int)((cu - 2 * (int64_t)p.Np - p.F) / 2);
+    };
+    const int64_t total_cost = 2 * (int64_t)p.Np + p.F + 2 * (int64_t)p.n_dec;
+    const int t0 = to_tok(min((int64_t)split * p.chunk, total_cost));
+    const int t1 = to_tok(min((int64_t)(split + 1) * p.chunk, total_cost));
     const int nv = min(max(__ldg(p.near_valid + s), 0), p.Np);
     Segs sg;
     sg.a[0] = t0;                       sg.e[0] = min(t1, nv);
@@ -997,33 +1005,63 @@ int num_sms() {
     return g_num_sms;
 }
 
+// Resident CTAs per SM of one decode kernel instantiation (queried once per
+// device after opting it into its dynamic shared memory).
+int resident_ctas(void (*kern)(DecodeParams), int smem) {
+    static thread_local std::vector<std::pair<std::pair<int, const void*>, int>> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 2;
+    for (auto& e : cache)
+        if (e.first.first == dev && e.first.second == (const void*)kern) return e.second;
+    int n = 2;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem) != cudaSuccess || n < 1)
+        n = 2;
+    cache.push_back({{dev, (const void*)kern}, n});
+    return n;
+}
+
+int resident_for(const FkvDecodeShape* sh, bool turbo) {
+    if (turbo)
+        return sh->D == 128 ? resident_ctas(decode_fp8_kernel<128, kTurbo>, Ring<128, kTurbo>::BYTES)
+                            : resident_ctas(decode_fp8_kernel<64, kTurbo>, Ring<64, kTurbo>::BYTES);
+    if (sh->D == 128)
+        return sh->v_group == 0 ? resident_ctas(decode_fp8_kernel<128, 0>, Ring<128, 0>::BYTES)
+                                : resident_ctas(decode_fp8_kernel<128, 32>, Ring<128, 32>::BYTES);
+    return sh->v_group == 0 ? resident_ctas(decode_fp8_kernel<64, 0>, Ring<64, 0>::BYTES)
+                            : resident_ctas(decode_fp8_kernel<64, 32>, Ring<64, 32>::BYTES);
+}
+
 struct Plan {
     int HG, splits, chunk;
     size_t rec_bytes, ticket_bytes;
     size_t qproj_bytes;   // turbo only: (B*Hq, 2D) f32 after the counters
 };
 
-Plan make_plan(const FkvDecodeShape* sh) {
+Plan make_plan(const FkvDecodeShape* sh, int resident) {
     Plan pl{};
     const int G = sh->Hq / sh->Hk;
     pl.HG = (G + kHeadsPerTile - 1) / kHeadsPerTile;
-    const int64_t T = (int64_t)sh->n_near_alloc + sh->n_far + sh->n_dec;
+    // work of a (b, kv head) stream in cost units: fp16 near / decode tokens
+    // take about twice as long as compressed far tokens
+    const int64_t T = 2 * (int64_t)sh->n_near_alloc + sh->n_far + 2 * (int64_t)sh->n_dec;
     const int64_t streams = (int64_t)sh->B * sh->Hk * pl.HG;
     int splits = sh->num_splits;
     if (splits <= 0) {
         // Pick the split count minimising (waves of resident CTAs) x (chunk
-        // length + a fixed per-CTA cost of ~384 tokens: pipeline fill, record
-        // write and merge).  Balances wave quantisation against CTA overhead:
+        // length + a fixed per-CTA cost of ~512 tokens: q fragments, pipeline
+        // fill, record write) + ~48 tokens per split record the last CTA of a
+        // stream merges.  Balances wave quantisation against CTA overhead:
         // few long CTAs for a handful of (b, kv head) streams, a few splits
         // for large batches.
-        const int64_t slots = (int64_t)num_sms() * 2;
+        const int64_t slots = (int64_t)num_sms() * std::max(resident, 1);
         double best = 1e300;
         splits = 1;
         for (int sp = 1; sp <= 64; ++sp) {
             const int64_t chunk_tok = (T + sp - 1) / sp;
             if (sp > 1 && chunk_tok < 256) break;
             const int64_t waves = (streams * sp + slots - 1) / slots;
-            const double cost = (double)waves * (double)(chunk_tok + 384);
+            const double cost = (double)waves * (double)(chunk_tok + 512) + 48.0 * sp;
             if (cost < best * 0.999) {
                 best = cost;
                 splits = sp;
@@ -1081,7 +1119,7 @@ int launch_kernel(void (*kern)(DecodeParams), int smem, dim3 grid, const DecodeP
 
 int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws_bytes,
            cudaStream_t st, bool turbo = false) {
-    const Plan pl = make_plan(sh);
+    const Plan pl = make_plan(sh, resident_for(sh, turbo));
     const size_t qoff = (pl.ticket_bytes + 255) & ~(size_t)255;
     const size_t front = turbo ? qoff + pl.qproj_bytes : pl.ticket_bytes;
     const size_t need = pl.rec_bytes + front + 256;
@@ -1152,7 +1190,10 @@ extern "C" {
 
 size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s) {
     if (validate(s) != FKV_OK) return 0;
-    const Plan pl = make_plan(s);
+    // enough for either far-tier kind (their resident counts, hence split
+    // counts, may differ)
+    const Plan a = make_plan(s, resident_for(s, false)), b = make_plan(s, resident_for(s, true));
+    const Plan& pl = a.rec_bytes >= b.rec_bytes ? a : b;
     return pl.rec_bytes + pl.ticket_bytes + 256 + ((pl.qproj_bytes + 255) & ~(size_t)255) + 256;
 }
 
@@ -1285,7 +1326,7 @@ extern "C" int fkv_decode_fp8_noalloc(const FkvDecodeShape* sh, const uint16_t* 
     fkv::clear_error();
     int rc = validate(sh);
     if (rc) return rc;
-    const Plan pl = make_plan(sh);
+    const Plan pl = make_plan(sh, resident_for(sh, false));
     const size_t need = pl.rec_bytes + pl.ticket_bytes + 256;
     FKV_REQUIRE(need <= kNoAllocScratchBytes, FKV_ERR_INVALID,
                 "fkv_decode_fp8_noalloc: shape needs %zu scratch bytes, above the fixed "
