@@ -213,13 +213,13 @@ def main_seqsplit(args, rank, world, device):
     import torch
     import torch.distributed as dist
     from foveated_kv_b200 import TierConfig
-    from foveated_kv_b200.seqsplit import shard_bounds, compress_shard, decode_seqsplit
+    from foveated_kv_b200.seqsplit import shard_bounds_balanced, compress_shard, decode_seqsplit
     from foveated_kv_b200.synthetic import torch_workload, CONFIGS
     c = CONFIGS["c4"]
     B, Hq, Hk, D, S = c["B"], c["Hq"], c["Hk"], c["D"], c["S"]
     cfg = TierConfig(near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
                      spike_margin=0.5)
-    lo, hi = shard_bounds(S, rank, world)
+    lo, hi = shard_bounds_balanced(S, rank, world, cfg)
     w = torch_workload(4000 + rank, B, Hk, Hq, hi - lo, D, 0, device)
     g = torch.Generator(device=device)
     g.manual_seed(77)
@@ -233,8 +233,19 @@ def main_seqsplit(args, rank, world, device):
     torch.cuda.synchronize()
     compress_ms = e0.elapsed_time(e1)
     del w
-    for _ in range(max(args.warmup, 3)):
+    # one step (partial kernel, NCCL all-gather, combine kernel) captured in a
+    # CUDA graph, replayed per step
+    gs = torch.cuda.Stream(device)
+    with torch.cuda.stream(gs):
+        for _ in range(max(args.warmup, 3)):
+            decode_seqsplit(lay, q, off)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=gs):
         decode_seqsplit(lay, q, off)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        graph.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -242,7 +253,7 @@ def main_seqsplit(args, rank, world, device):
     with ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) as clk:
         e0.record()
         for _ in range(args.steps):
-            decode_seqsplit(lay, q, off)
+            graph.replay()
         e1.record()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
@@ -292,7 +303,9 @@ def main_seqsplit(args, rank, world, device):
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic (seeded N(0,1) fp16)",
             "config": {"workload": "c4", "B": B, "Hq": Hq, "Hk": Hk, "D": D, "S": S,
-                       "near_pct": c["near_pct"], "parallelism": f"sequence split x{world}",
+                       "near_pct": c["near_pct"],
+                       "parallelism": f"sequence split x{world} (equal-cost shards)",
+                       "shard": [lo, hi],
                        "exchange": "NCCL all-gather of (m, l, o) records + combine kernel"},
             "us_per_layer": ms * 1e3, "compress_ms": compress_ms,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

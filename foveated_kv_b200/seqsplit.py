@@ -1,8 +1,9 @@
 """Sequence-split decode across GPUs (long contexts; no reference counterpart:
 the reference has no multi-device code).
 
-The prefill sequence [0, S) is split evenly into world_size shards of
-positions.  Each rank tiers its shard with the GLOBAL recency tier boundaries
+The prefill sequence [0, S) is split into world_size contiguous shards of
+positions (``shard_bounds``: equal length; ``shard_bounds_balanced``: equal
+decode cost).  Each rank tiers its shard with the GLOBAL recency tier boundaries
 (a position is near or far exactly as in the unsplit cache), runs the fused
 decode kernel in partial mode (one (m, l, o, min_near, max_far, argmax)
 record per (b, q head), argmax as a global far index), all-gathers the
@@ -30,6 +31,23 @@ def shard_bounds(S: int, rank: int, world: int):
     base, rem = divmod(S, world)
     lo = rank * base + min(rank, rem)
     return lo, lo + base + (1 if rank < rem else 0)
+
+
+def shard_bounds_balanced(S: int, rank: int, world: int, cfg: TierConfig):
+    """Split [0, S) into `world` contiguous shards of equal decode cost: an
+    fp16 near token costs 2 (K+V at 2 bytes/element), a compressed far token
+    1.  The global near tier (sinks, recent middle, window) sits at the two
+    ends of the sequence, so equal-length shards leave the last rank with most
+    of the fp16 rows."""
+    if world == 1:
+        return 0, S
+    tb = cfg.tier_boundaries(S)
+    cost = np.ones(S, dtype=np.int64)
+    cost[:tb["n_sinks"]] = 2
+    cost[tb["near_mid_start"]:] = 2
+    cum = np.concatenate([[0], np.cumsum(cost)])
+    cuts = [0] + [int(np.searchsorted(cum, cum[-1] * r / world)) for r in range(1, world)] + [S]
+    return cuts[rank], cuts[rank + 1]
 
 
 def shard_positions(S: int, lo: int, hi: int, cfg: TierConfig):
