@@ -233,19 +233,21 @@ def main_seqsplit(args, rank, world, device):
     torch.cuda.synchronize()
     compress_ms = e0.elapsed_time(e1)
     del w
-    # one step (partial kernel, NCCL all-gather, combine kernel) captured in a
-    # CUDA graph, replayed per step
-    gs = torch.cuda.Stream(device)
-    with torch.cuda.stream(gs):
-        for _ in range(max(args.warmup, 3)):
+    # one GPU: the step (partial + combine kernels) is captured in a CUDA
+    # graph; several GPUs: eager steps (the NCCL all-gather is not captured)
+    graph = None
+    if world == 1:
+        gs = torch.cuda.Stream(device)
+        with torch.cuda.stream(gs):
+            for _ in range(max(args.warmup, 3)):
+                decode_seqsplit(lay, q, off)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=gs):
             decode_seqsplit(lay, q, off)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=gs):
-        decode_seqsplit(lay, q, off)
-    torch.cuda.synchronize()
-    for _ in range(3):
-        graph.replay()
+    step = graph.replay if graph is not None else (lambda: decode_seqsplit(lay, q, off))
+    for _ in range(max(args.warmup, 3)):
+        step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -253,7 +255,7 @@ def main_seqsplit(args, rank, world, device):
     with ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) as clk:
         e0.record()
         for _ in range(args.steps):
-            graph.replay()
+            step()
         e1.record()
         torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / args.steps
