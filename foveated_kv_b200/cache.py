@@ -210,6 +210,34 @@ class FoveatedLayer:
         reference's dequantise-then-SDPA path is not kept in the product)."""
         return self.attend_fused(query)
 
+    # ---- alternative spike policy (mlx_foveated.py:451-499) -----------------------
+    def detect_spikes(self, query: torch.Tensor, margin: float = 0.5) -> Optional[torch.Tensor]:
+        """GQA-mean query spike check (``detect_spikes``, mlx_foveated.py:451-490).
+
+        q = mean of the group's query heads; a far token spikes when its
+        score exceeds the lowest near / decode score + margin.  Returns an
+        int32 (N, 3) tensor of [b, kv head, far-local argmax] for the heads
+        with any spike, or None.  An auxiliary policy outside the fused
+        kernel: plain torch ops on the layer's tensors.
+        """
+        if self.compress_method != "fp8" or self.n_far == 0:
+            return None
+        D = query.shape[-1]
+        q = query.reshape(query.shape[0], query.shape[1], D).float()
+        G = q.shape[1] // self.H_kv
+        q = q.reshape(q.shape[0], self.H_kv, G, D).mean(2)                   # (B, H, D)
+        near = self.effective_near_k.float()
+        near_s = torch.einsum("bhd,bhtd->bht", q, near) / math.sqrt(D)
+        thr = near_s.min(dim=-1, keepdim=True).values + margin
+        far = self.far_k.view(torch.float8_e4m3fn).to(torch.float16).float()
+        far_s = torch.einsum("bhd,bhtd->bht", q, far) / math.sqrt(D)
+        mask = (far_s > thr).any(dim=-1)
+        if not bool(mask.any()):
+            return None
+        bh = mask.nonzero()
+        best = far_s.argmax(dim=-1)[bh[:, 0], bh[:, 1]]
+        return torch.stack([bh[:, 0], bh[:, 1], best], 1).to(torch.int32)
+
     # ---- promotion target (foveated_attn.cpp:242-254) ---------------------------
     def get_blob_info(self) -> dict:
         return {"near_k": self.near_k, "near_v": self.near_v, "near_valid": self.near_valid,
@@ -329,12 +357,47 @@ class FoveatedKVCache:
             self._prefill_values[layer_idx] = torch.cat(
                 [self._prefill_values[layer_idx], value_states], 2)
 
+    def compress_async(self, layer_idx: int, stream: Optional[torch.cuda.Stream] = None,
+                       query=None, keep_archive: bool = True) -> torch.cuda.Event:
+        """Tier one layer on a side stream as soon as its prefill K/V is
+        complete, so the compression overlaps the next layer's prefill on the
+        main stream.  Returns an event recorded after the layer's compression;
+        ``compress()`` (or ``synchronize_compression``) waits for all of them."""
+        k, v = self._prefill_keys[layer_idx], self._prefill_values[layer_idx]
+        main = torch.cuda.current_stream(k.device)
+        side = stream or torch.cuda.Stream(k.device)
+        side.wait_stream(main)                       # K/V were produced on main
+        with torch.cuda.stream(side):
+            lay = compress_layer(k, v, self.cfg, query, keep_archive)
+        k.record_stream(side)
+        v.record_stream(side)
+        ev = torch.cuda.Event()
+        ev.record(side)
+        self.layers[layer_idx] = lay
+        self._pending = getattr(self, "_pending", {})
+        self._pending[layer_idx] = (ev, k.numel() * k.element_size() * 2, k.shape[2])
+        self._prefill_keys[layer_idx] = None
+        self._prefill_values[layer_idx] = None
+        return ev
+
+    def synchronize_compression(self) -> None:
+        """Make the current stream wait for every ``compress_async`` layer."""
+        for ev, _, _ in getattr(self, "_pending", {}).values():
+            torch.cuda.current_stream().wait_event(ev)
+
     def compress(self, query=None, keep_archive: bool = True) -> dict:
         """Compress all layers.  ``query``: observation query for importance
         selection -- one (B, Hq, D) tensor for every layer, or a per-layer list."""
-        if not self._prefill_keys:
+        pending = getattr(self, "_pending", {})
+        if not self._prefill_keys and not pending:
             return {"compressed": False}
+        self.synchronize_compression()
         before = after = 0
+        for i, (_, nbytes, S) in pending.items():
+            before += nbytes
+            after += self.layers[i].memory_bytes()["total_quantized"]
+            self.seq_length = S
+        self._pending = {}
         for i, (k, v) in enumerate(zip(self._prefill_keys, self._prefill_values)):
             if k is None:
                 continue

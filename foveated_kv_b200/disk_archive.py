@@ -44,6 +44,14 @@ class DiskArchive:
         v = torch.from_numpy(np.array(self.mmap_v[b, head, ix]))
         return k.reshape(1, 1, n, self.D), v.reshape(1, 1, n, self.D)
 
+    def score_boundary_tokens(self, head: int, query, token_indices, b: int = 0) -> np.ndarray:
+        """Scores k . q of archived tokens for host-side rescoring
+        (disk_archive.py:89-109): (N,) float32."""
+        if len(token_indices) == 0:
+            return np.array([], dtype=np.float32)
+        k = np.asarray(self.mmap_k[b, head, np.asarray(token_indices)], dtype=np.float32)
+        return k @ np.asarray(query, dtype=np.float32)
+
     def memory_bytes_in_ram(self) -> int:
         return self.idx.numel() * self.idx.element_size()
 
