@@ -175,8 +175,11 @@ class FoveatedLayer:
             q = q.to(F16).contiguous()
         margin = self.spike_margin if spike_margin is None else float(spike_margin)
         sh = self._fill_shape(Hq, margin)
-        ws_bytes = lib.fkv_decode_workspace_bytes(C.byref(sh))
-        ws = _Workspace.get(ws_bytes, self.device)
+        key = (Hq, self._n_dec, sh.dec_stride)
+        if getattr(self, "_ws_key", None) != key:      # plan changes only with these
+            self._ws_key = key
+            self._ws_bytes = lib.fkv_decode_workspace_bytes(C.byref(sh))
+        ws = _Workspace.get(self._ws_bytes, self.device)
         if out is None:
             out = torch.empty((B, Hq, 1, D), dtype=F16, device=self.device)
         flags = torch.empty((B, Hq), dtype=I32, device=self.device)
