@@ -68,3 +68,15 @@ def test_missing_library_raises(tmp_path, monkeypatch):
     monkeypatch.setattr(_native, "_lib", None)
     with pytest.raises(_native.FkvNativeError):
         _native.load(str(tmp_path / "nope.so"))
+
+
+def test_shape_limits_rejected_before_any_cuda_call():
+    lib = _native.load()
+    sh = _native.DecodeShape(B=70000, Hq=8, Hk=1, D=128)      # B*Hk beyond the grid limit
+    assert lib.fkv_decode_fp8(C.byref(sh), *([None] * 14), 0, None) == -2
+    sh = _native.DecodeShape(B=1, Hq=8, Hk=2, D=128, n_near_alloc=10, n_far=5, n_dec=4, dec_stride=2)
+    assert lib.fkv_decode_fp8(C.byref(sh), *([None] * 14), 0, None) == -1   # n_dec > capacity
+    assert lib.fkv_decode_workspace_bytes(C.byref(sh)) == 0
+    L = _native.TierLayout()
+    assert lib.fkv_compress_fp8(C.byref(L), 1, 1, 96, None, None, 0, None, None, 0,
+                                *([None] * 8), None) == -2          # head dim 96 unsupported
