@@ -205,6 +205,21 @@ def reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+
+def qk_path_name(lay, Hq: int) -> str:
+    """The q.K path the fused decode takes for this layer (reported in config)."""
+    import ctypes as C
+    import torch
+    from foveated_kv_b200 import _native
+    if lay.far_k is None or lay.n_far == 0 or lay.far_k.dtype != torch.uint8:
+        return "mma.sync"
+    if lay.far_k.shape[-1] != lay.near_k.shape[-1]:
+        return "mma.sync (TurboQuant codes)"
+    lib = _native.load()
+    sh = lay._fill_shape(Hq, lay.spike_margin)
+    nh = lib.fkv_decode_qk_path(C.byref(sh), lay.far_k.data_ptr())
+    return f"tcgen05.mma f8f6f4 ({nh} q heads/CTA)" if nh > 0 else "mma.sync"
+
 def main_seqsplit(args, rank, world, device):
     """c4: one 1M-token sequence split evenly over the ranks; per step each
     rank decodes its shard in partial mode, the (m, l, o) records are
@@ -308,7 +323,8 @@ def main_seqsplit(args, rank, world, device):
                        "near_pct": c["near_pct"],
                        "parallelism": f"sequence split x{world} (equal-cost shards)",
                        "shard": [lo, hi],
-                       "exchange": "NCCL all-gather of (m, l, o) records + combine kernel"},
+                       "exchange": "NCCL all-gather of (m, l, o) records + combine kernel",
+                       "qk_path": qk_path_name(lay, Hq)},
             "us_per_layer": ms * 1e3, "compress_ms": compress_ms,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "algorithmic_bytes_per_launch": alg_total / world,
@@ -451,7 +467,8 @@ def main():
                                     "fp8 E4M3 K + INT4 V (" + ("per token" if c["v_group"] is None
                                                               else "group 32") + ")"),
                        "global_batch": B * world, "parallelism": f"batch-shard x{world}",
-                       "l2": "inputs larger than L2 (no flush)"},
+                       "l2": "inputs larger than L2 (no flush)",
+                       "qk_path": qk_path_name(lay, Hq)},
             "us_per_layer": ms * 1e3, "hbm_gbs": achieved,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_src,

@@ -63,6 +63,7 @@ SIGNATURES = {
     "fkv_compress_turbo": (C.c_int, [C.POINTER(TierLayout), I32, I32, I32, P, P, I64, P, P,
                                      P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
     "fkv_decode_workspace_bytes": (SZ, [C.POINTER(DecodeShape)]),
+    "fkv_decode_qk_path": (C.c_int, [C.POINTER(DecodeShape), P]),
     "fkv_decode_fp8": (C.c_int, [C.POINTER(DecodeShape), P, P, P, P, P, P, P, P, P, P, P, P,
                                  P, P, SZ, P]),
     "fkv_decode_turbo": (C.c_int, [C.POINTER(DecodeShape), P, P, P, P, P, P, P, P, P, P, P,

@@ -9,12 +9,16 @@
 // Unlike the Metal kernel every (b, kv head) is read once for all its q heads
 // (GQA group on the tensor-core M dimension) and no score-gated V skip is
 // applied (the output matches dequantise-then-attend without the exp(-16) cut).
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -72,11 +76,62 @@ struct RecLayout {
     static constexpr int SIZE = 40 + 8 * D;   // floats
 };
 
+// q pieces of the tensor-core far path from a lane's scaled q values: lane
+// (r, c) holds head r of the CTA's group (zero when absent), dims
+// [c*D/4, (c+1)*D/4).  With e = 2^E chosen so that max|q| e lies in
+// [128, 256), piece 0 = e4m3(q e) and piece j+1 = e4m3(16 (r_j - piece_j)) of
+// the residual r_j; then q = sum_j piece_j 16^-j / e up to 2^-16 relative per
+// element, and a score is (acc_0 + acc_1/16 + acc_2/256 + acc_3/4096) / e.
+// Piece j of head r is row j*NH + r of the B operand (K-major rows of D bytes
+// in the 128-byte swizzle).
+constexpr int kQPieces = 4;
+
+template <int D, int NH>
+__device__ __forceinline__ void build_q_pieces_from(const float (&qv)[D / 4], int lane,
+                                                    uint8_t* __restrict__ qb, float* escale) {
+    static_assert(D == 128, "tensor-core far path assumes 128-byte K rows");
+    constexpr int KC = D / 4;
+    const int r = lane >> 2, c = lane & 3;
+    float mx = 0.f;
+#pragma unroll
+    for (int u = 0; u < KC; ++u) mx = fmaxf(mx, fabsf(qv[u]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    int ex = 0;
+    frexpf(mx, &ex);                                  // mx < 2^ex
+    const float sc = mx > 0.f ? ldexpf(1.f, 8 - ex) : 1.f;
+    if (lane == 0) *escale = 1.f / sc;                // exact: a power of two
+    if (r >= NH) return;
+#pragma unroll
+    for (int v = 0; v < KC / 4; ++v) {
+        const int d0 = c * KC + 4 * v;
+        float rv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) rv[e] = qv[4 * v + e] * sc;
+#pragma unroll
+        for (int j = 0; j < kQPieces; ++j) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const __nv_fp8_storage_t code = __nv_cvt_float_to_fp8(rv[e], __NV_SATFINITE, __NV_E4M3);
+                word |= (uint32_t)code << (8 * e);
+                const float back = __half2float(__half(__nv_cvt_fp8_to_halfraw(code, __NV_E4M3)));
+                rv[e] = (rv[e] - back) * 16.f;      // exact residual, scaled up
+            }
+            const int n = j * NH + r;               // B row
+            *reinterpret_cast<uint32_t*>(qb + n * 128 + ((((d0 >> 4) ^ (n & 7)) << 4) | (d0 & 15))) = word;
+        }
+    }
+}
+
 // q A-fragments of the CTA's head group, one uint4 per (k-step, lane), built
 // once by consumer warp 0 into shared memory and read by every consumer warp
-template <int D>
+// With NH > 0 the same registers also give the tensor-core far path's q
+// pieces (build_q_pieces_from).
+template <int D, int NH = 0>
 __device__ __forceinline__ void build_q_frags(const DecodeParams& p, int s, int hg, int lane,
-                                              uint4* __restrict__ qs) {
+                                              uint4* __restrict__ qs, uint8_t* __restrict__ qb = nullptr,
+                                              float* escale = nullptr) {
     const int r = lane >> 2, c = lane & 3;
     const int b = s / p.Hk, h = s % p.Hk;
     const int g = hg * kHeadsPerTile + r;
@@ -98,6 +153,7 @@ __device__ __forceinline__ void build_q_frags(const DecodeParams& p, int s, int 
 #pragma unroll
         for (int u = 0; u < KC; ++u) qv[u] = 0.f;
     }
+    if constexpr (NH > 0) build_q_pieces_from<D, NH>(qv, lane, qb, escale);
 #pragma unroll
     for (int j = 0; j < D / 16; ++j) {
         __half hi[4], lo[4];
@@ -140,6 +196,28 @@ struct Ring {
     static constexpr int TSUM = QOFF + (VG == kTurbo ? 3 : 1) * QFRAG;   // turbo row sums
     static constexpr int BAROFF = TSUM + (VG == kTurbo ? 64 : 0);        // mbarriers
     static constexpr int BYTES = BAROFF + 2 * kStages * 8;
+};
+
+// Extra shared memory of the tensor-core far path (placed after the ring's
+// layout): the q-piece B operand (1024-byte aligned for the 128-byte
+// swizzle), the MMA-done / q-ready / drain mbarriers, the TMEM base address and
+// the piece scale.  The dynamic shared memory base is rounded up to 1024 bytes
+// in the kernel, hence the slack.
+template <int D, int VG>
+struct UmLayout {
+    using RG = Ring<D, VG>;
+    static constexpr int QB = (RG::BYTES + 1023) & ~1023;
+    static constexpr int MMAB = QB + 4 * kHeadsPerTile * 128;   // kStages MMA-done barriers
+    static constexpr int QREADY = MMAB + kStages * 8;
+    static constexpr int DRAIN = QREADY + 8;
+    static constexpr int TADDR = DRAIN + 8;
+    static constexpr int ESC = TADDR + 4;
+    static constexpr int BYTES = ESC + 4 + 1024;
+    static constexpr uint32_t TMEM_COLS = 64;   // kStages x 32 score columns
+    static_assert(RG::SLOT % 1024 == 0, "ring slots must keep 1024-byte alignment");
+    static_assert(MMAB < QREADY && QREADY < DRAIN && DRAIN < TADDR && TADDR < ESC && ESC < BYTES &&
+                      TMEM_COLS == kStages * 32,
+                  "layout order");
 };
 
 // Bytes [b0, b1) of `base` (an array of `total` bytes) into shared `dst`,
@@ -260,40 +338,16 @@ __device__ __forceinline__ void load_sz(const uint16_t* __restrict__ sc,
     }
 }
 
-// ---- NT 16-token tiles of an fp8 / INT4 far stage, processed jointly ----
-// (the tiles' loads, conversions and tensor-core products are interleaved and
-// share one online-softmax step, which gives each warp instruction-level
-// parallelism at the occupancy the register budget allows)
-template <int D, int VG, int NT>
-__device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
-                                          const uint8_t* __restrict__ vbuf, const int (&u0)[NT],
-                                          int cnt, int gbase, int lane,
-                                          const uint4* __restrict__ qs,
-                                          const uint32_t (&sz)[NT][4], WarpState<D>& st) {
-    constexpr int KW = D / 16;    // u32 words of fp8 K per lane per token (D/4 bytes)
+// INT4 V words of NT far tiles in the V^T A-fragment order (lane r: dims
+// [r*D/8, (r+1)*D/8) of tokens u0[t] + {2c, 2c+1, 8+2c, 9+2c})
+template <int D, int NT>
+__device__ __forceinline__ void load_far_v(const uint8_t* __restrict__ vbuf, const int (&u0)[NT],
+                                           int cnt, int lane,
+                                           uint32_t (&vr)[NT][4][(D / 16 + 3) / 4]) {
     constexpr int VB = D / 16;    // bytes of INT4 V per lane per token (D/8 dims)
-    constexpr int VWN = (VB + 3) / 4;
     const int r = lane >> 2, c = lane & 3;
-    uint32_t kr[NT][2][KW];
-    uint32_t vr[NT][4][VWN];
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
-            const int u = u0[t] + 8 * n + r;
-            const uint4* src = reinterpret_cast<const uint4*>(kbuf + u * D + c * (D / 4));
-            if constexpr (KW == 8) {
-                // odd rows read their second 16 bytes first: conflict-free phases
-                const int f = r & 1;
-                const uint4 w0 = src[f], w1 = src[f ^ 1];
-                const uint4 lo = f ? w1 : w0, hi = f ? w0 : w1;
-                kr[t][n][0] = lo.x; kr[t][n][1] = lo.y; kr[t][n][2] = lo.z; kr[t][n][3] = lo.w;
-                kr[t][n][4] = hi.x; kr[t][n][5] = hi.y; kr[t][n][6] = hi.z; kr[t][n][7] = hi.w;
-            } else {
-                const uint4 w = src[0];
-                kr[t][n][0] = w.x; kr[t][n][1] = w.y; kr[t][n][2] = w.z; kr[t][n][3] = w.w;
-            }
-        }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const int u = u0[t] + (e >> 1) * 8 + 2 * c + (e & 1);
@@ -308,32 +362,24 @@ __device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
             }
         }
     }
-    float sc[NT][2][4];
-#pragma unroll
-    for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int n = 0; n < 2; ++n) sc[t][n][0] = sc[t][n][1] = sc[t][n][2] = sc[t][n][3] = 0.f;
-#pragma unroll
-    for (int j = 0; j < D / 16; ++j) {
-        const uint4 qv = qs[j * 32 + lane];
-        const uint32_t qa[4] = {qv.x, qv.y, qv.z, qv.w};
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-#pragma unroll
-            for (int n = 0; n < 2; ++n) {
-                uint32_t b0, b1;
-                e4m3x4_to_h2x2(kr[t][n][j], b0, b1);
-                mma16816(sc[t][n], qa, b0, b1);
-            }
-        }
-    }
+}
+
+// Masking, spike tracking, online softmax and the P.V product of NT far
+// tiles whose raw scores `sv` are in the S C-fragment layout (lane (r, c):
+// head r, tokens u0[t] + {2c, 2c+1, 8+2c, 9+2c}) and whose V words are in vr.
+template <int D, int VG, int NT>
+__device__ __forceinline__ void far_tail(const float (&sv)[4 * NT],
+                                         const uint32_t (&vr)[NT][4][(D / 16 + 3) / 4],
+                                         const int (&u0)[NT], int cnt, int gbase, int lane,
+                                         const uint32_t (&sz)[NT][4], WarpState<D>& st) {
+    const int c = lane & 3;
     float s[4 * NT], pr[4 * NT];
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int u = u0[t] + (j >> 1) * 8 + 2 * c + (j & 1);
-            const float v = sc[t][j >> 1][j & 1] + sc[t][j >> 1][2 + (j & 1)];
+            const float v = sv[4 * t + j];
             s[4 * t + j] = u < cnt ? v : -INFINITY;
             if (u < cnt && v > st.mf) {   // lane's tokens arrive in increasing order
                 st.mf = v;
@@ -392,6 +438,128 @@ __device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
             }
         }
     }
+}
+
+// ---- NT 16-token tiles of an fp8 / INT4 far stage, processed jointly ----
+// (the tiles' loads, conversions and tensor-core products are interleaved and
+// share one online-softmax step, which gives each warp instruction-level
+// parallelism at the occupancy the register budget allows)
+template <int D, int VG, int NT>
+__device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
+                                          const uint8_t* __restrict__ vbuf, const int (&u0)[NT],
+                                          int cnt, int gbase, int lane,
+                                          const uint4* __restrict__ qs,
+                                          const uint32_t (&sz)[NT][4], WarpState<D>& st) {
+    constexpr int KW = D / 16;    // u32 words of fp8 K per lane per token (D/4 bytes)
+    constexpr int VWN = (D / 16 + 3) / 4;
+    const int r = lane >> 2, c = lane & 3;
+    uint32_t kr[NT][2][KW];
+    uint32_t vr[NT][4][VWN];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+            const int u = u0[t] + 8 * n + r;
+            const uint4* src = reinterpret_cast<const uint4*>(kbuf + u * D + c * (D / 4));
+            if constexpr (KW == 8) {
+                // odd rows read their second 16 bytes first: conflict-free phases
+                const int f = r & 1;
+                const uint4 w0 = src[f], w1 = src[f ^ 1];
+                const uint4 lo = f ? w1 : w0, hi = f ? w0 : w1;
+                kr[t][n][0] = lo.x; kr[t][n][1] = lo.y; kr[t][n][2] = lo.z; kr[t][n][3] = lo.w;
+                kr[t][n][4] = hi.x; kr[t][n][5] = hi.y; kr[t][n][6] = hi.z; kr[t][n][7] = hi.w;
+            } else {
+                const uint4 w = src[0];
+                kr[t][n][0] = w.x; kr[t][n][1] = w.y; kr[t][n][2] = w.z; kr[t][n][3] = w.w;
+            }
+        }
+    }
+    load_far_v<D, NT>(vbuf, u0, cnt, lane, vr);
+    float sc[NT][2][4];
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int n = 0; n < 2; ++n) sc[t][n][0] = sc[t][n][1] = sc[t][n][2] = sc[t][n][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < D / 16; ++j) {
+        const uint4 qv = qs[j * 32 + lane];
+        const uint32_t qa[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+#pragma unroll
+            for (int n = 0; n < 2; ++n) {
+                uint32_t b0, b1;
+                e4m3x4_to_h2x2(kr[t][n][j], b0, b1);
+                mma16816(sc[t][n], qa, b0, b1);
+            }
+        }
+    }
+    float sv[4 * NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sv[4 * t + j] = sc[t][j >> 1][j & 1] + sc[t][j >> 1][2 + (j & 1)];
+    far_tail<D, VG, NT>(sv, vr, u0, cnt, gbase, lane, sz, st);
+}
+
+// ---- far tiles scored on the 5th-generation tensor cores (tcgen05) ----
+// The producer lane issues, per 128-token far stage, S^T = K . Qp^T with
+// tcgen05.mma kind::f8f6f4: A = the stage's E4M3 K codes exactly as stored
+// (128 tokens x D bytes, loaded by a tensor-map TMA copy in the 128-byte
+// swizzle), B = Qp, the CTA's q heads split into four E4M3 pieces, f32
+// accumulators in tensor memory (TMEM lane = token, column = piece * NH +
+// head).  No K conversion runs on the SM cores.  Consumer warp w owns TMEM
+// lanes / tokens [32w, 32w + 32): it loads its rows, folds the pieces,
+// transposes the scores through shared memory into the S C-fragment layout
+// and continues with far_tail (softmax, INT4 V on mma.sync).
+
+// floats per head row of the score transpose buffer (row r at bank offset 8r:
+// conflict-free float2 reads)
+constexpr int kTsStride = 40;
+
+// Returns false when the MMA-done barrier `mmab` (phase `parity`) timed out.
+template <int D, int VG, int NT, int NH>
+__device__ __forceinline__ bool far_tiles_um(uint8_t* __restrict__ kbuf,
+                                             const uint8_t* __restrict__ vbuf, const int (&u0)[NT],
+                                             int cnt, int gbase, int lane, int w, uint32_t taddr,
+                                             float escale, uint64_t* mmab, uint32_t parity,
+                                             const uint32_t (&sz)[NT][4], WarpState<D>& st) {
+    constexpr int VWN = (D / 16 + 3) / 4;
+    const int r = lane >> 2, c = lane & 3;
+    uint32_t vr[NT][4][VWN];
+    load_far_v<D, NT>(vbuf, u0, cnt, lane, vr);   // V loads overlap the MMA wait
+    if (!mbar_wait(mmab, parity)) return false;
+    tc_fence_after();
+    uint32_t acc[kQPieces * NH];
+    if constexpr (NH == 4) tmem_ld16(taddr, acc);
+    else tmem_ld32(taddr, acc);
+    tmem_wait_ld();
+    // the stage's K codes were consumed by the MMA: its K region is free for
+    // the per-warp transpose [head][token]
+    float* tb = reinterpret_cast<float*>(kbuf) + w * (NH * kTsStride);
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) {
+        float v = __uint_as_float(acc[hh]);
+        v = fmaf(__uint_as_float(acc[NH + hh]), 0.0625f, v);
+        v = fmaf(__uint_as_float(acc[2 * NH + hh]), 0.00390625f, v);
+        v = fmaf(__uint_as_float(acc[3 * NH + hh]), 0.000244140625f, v);
+        tb[hh * kTsStride + lane] = v * escale;
+    }
+    __syncwarp();
+    float sv[4 * NT];
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+            float2 v2 = make_float2(0.f, 0.f);      // rows r >= NH: no q head (zero q)
+            if (r < NH)
+                v2 = *reinterpret_cast<const float2*>(tb + r * kTsStride + (u0[t] & 31) + 8 * x + 2 * c);
+            sv[4 * t + 2 * x] = v2.x;
+            sv[4 * t + 2 * x + 1] = v2.y;
+        }
+    }
+    far_tail<D, VG, NT>(sv, vr, u0, cnt, gbase, lane, sz, st);
+    return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -674,11 +842,20 @@ __device__ __forceinline__ void merge_and_emit(const DecodeParams& p, const floa
     }
 }
 
-template <int D, int VG>
-__global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodeParams p) {
+// NH = 0: far-tier q.K on mma.sync after converting the codes; NH = 4 or 8:
+// far-tier q.K on tcgen05 (NH q heads per CTA, D = 128, E4M3 K; kmap is the
+// tensor map of far_k as (B*Hk*F rows, D bytes), unused when NH = 0).
+template <int D, int VG, int NH = 0>
+__global__ void __launch_bounds__(kThreads, 3)
+    decode_fp8_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap) {
     using R = RecLayout<D>;
     using RG = Ring<D, VG>;
-    extern __shared__ __align__(128) uint8_t smem[];
+    using UL = UmLayout<D, VG>;
+    constexpr bool UM = NH > 0;
+    static_assert(!UM || (D == 128 && VG != kTurbo), "tensor-core far path: fp8 K, D = 128");
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw;
+    if constexpr (UM) smem += (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + RG::BAROFF);
     uint4* qs = reinterpret_cast<uint4*>(smem + RG::QOFF);
     uint64_t* empty = full + kStages;
@@ -690,6 +867,11 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
         for (int i = 0; i < kStages; ++i) {
             mbar_init(full + i, 1);
             mbar_init(empty + i, kConsumerWarps);
+        }
+        if constexpr (UM) {
+            for (int i = 0; i < kStages; ++i) mbar_init(reinterpret_cast<uint64_t*>(smem + UL::MMAB) + i, 1);
+            mbar_init(reinterpret_cast<uint64_t*>(smem + UL::QREADY), 1);
+            mbar_init(reinterpret_cast<uint64_t*>(smem + UL::DRAIN), 1);
         }
         fence_mbar_init();
     }
@@ -725,18 +907,20 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
             const uint8_t* fv = p.far_v + (int64_t)s * p.F * (D / 2);
             const uint8_t* dk = reinterpret_cast<const uint8_t*>(p.dec_k) + (int64_t)s * p.dec_stride * D * 2;
             const uint8_t* dv = reinterpret_cast<const uint8_t*>(p.dec_v) + (int64_t)s * p.dec_stride * D * 2;
-            for (int k = 0; k < nstage; ++k) {
+            // copies of stage k into slot k % kStages, completing on full[slot]
+            auto issue = [&](int k) {
                 const int slot = k % kStages;
-                if (k >= kStages && !mbar_wait(empty + slot, ((k / kStages) - 1) & 1)) {
-                    atomicExch(p.status, FKV_ERR_TIMEOUT);
-                    break;
-                }
                 int seg, start, cnt;
                 stage_at<D>(sg, k, seg, start, cnt);
                 uint8_t* dst = smem + slot * RG::SLOT;
                 const uint8_t *ks, *vs;
                 uint32_t kb, vb;
-                if (seg == 1 && VG == kTurbo) {
+                if (seg == 1 && UM) {
+                    ks = nullptr;                                          // tensor-map copy below
+                    vs = fv + (int64_t)start * (D / 2);
+                    kb = RG::FAR_TOK * D;                                  // whole box, rows past
+                    vb = cnt * (D / 2);                                    // the stream are unused
+                } else if (seg == 1 && VG == kTurbo) {
                     ks = p.far_k + ((int64_t)s * p.F + start) * (D / 4);   // 2-bit key codes
                     vs = p.far_v + ((int64_t)s * p.F + start) * (D / 4);   // 2-bit value codes
                     kb = vb = cnt * (D / 4);
@@ -750,7 +934,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
                     vs = (seg == 0 ? nvp : dv) + (int64_t)start * D * 2;
                     kb = vb = cnt * D * 2;
                 }
-                bulk_g2s(dst, ks, kb, full + slot);
+                if (seg == 1 && UM) tma_load_2d(dst, &kmap, 0, (int)((int64_t)s * p.F + start), full + slot);
+                else bulk_g2s(dst, ks, kb, full + slot);
                 bulk_g2s(dst + RG::VOFF, vs, vb, full + slot);
                 uint32_t tx = kb + vb;
                 if (seg == 1) {
@@ -775,6 +960,77 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
                     }
                 }
                 mbar_arrive_expect_tx(full + slot, tx);
+            };
+            if constexpr (!UM) {
+                for (int k = 0; k < nstage; ++k) {
+                    if (k >= kStages && !mbar_wait(empty + k % kStages, ((k / kStages) - 1) & 1)) {
+                        atomicExch(p.status, FKV_ERR_TIMEOUT);
+                        break;
+                    }
+                    issue(k);
+                }
+            } else {
+                // Two event streams polled without blocking: refill a slot as
+                // soon as the consumers release it (copies run kStages ahead,
+                // as on the mma.sync path), and issue a far stage's MMA as
+                // soon as its data lands.  Idle polls back off with a short
+                // sleep; a long run of idle polls is a timeout.
+                uint64_t* mmab = reinterpret_cast<uint64_t*>(smem + UL::MMAB);
+                uint64_t* qready = reinterpret_cast<uint64_t*>(smem + UL::QREADY);
+                bool ok = true, any_mma = false, have_t = false;
+                uint32_t tbase = 0, idle = 0;
+                int kc = 0, km = 0;
+                while (km < nstage) {
+                    bool prog = false;
+                    if (km < kc && mbar_test(full + km % kStages, (km / kStages) & 1)) {
+                        const int slot = km % kStages;
+                        int seg, start, cnt;
+                        stage_at<D>(sg, km, seg, start, cnt);
+                        if (seg != 1) {
+                            mbar_arrive(mmab + slot);   // keeps the barrier's phase = stage use
+                            ++km;
+                            prog = true;
+                        } else if (have_t || mbar_test(qready, 0)) {
+                            if (!have_t) {
+                                tc_fence_after();
+                                tbase = *reinterpret_cast<volatile uint32_t*>(smem + UL::TADDR);
+                                have_t = true;
+                            }
+                            tc_fence_after();
+                            const uint32_t a0 = smem_u32(smem + slot * RG::SLOT);
+                            const uint32_t b0 = smem_u32(smem + UL::QB);
+                            constexpr uint32_t idesc = f8_idesc(128, kQPieces * NH);
+#pragma unroll
+                            for (int j = 0; j < D / 32; ++j)
+                                umma_f8(tbase + slot * 32, sw128_kmajor_desc(a0 + 32 * j),
+                                        sw128_kmajor_desc(b0 + 32 * j), idesc, j > 0);
+                            umma_commit(mmab + slot);
+                            any_mma = true;
+                            ++km;
+                            prog = true;
+                        }
+                    }
+                    if (kc < nstage &&
+                        (kc < kStages || mbar_test(empty + kc % kStages, ((kc / kStages) - 1) & 1))) {
+                        issue(kc);
+                        ++kc;
+                        prog = true;
+                    }
+                    if (prog) {
+                        idle = 0;
+                    } else if (++idle > kWaitLimit) {
+                        ok = false;
+                        break;
+                    } else {
+                        __nanosleep(32);
+                    }
+                }
+                if (!ok) atomicExch(p.status, FKV_ERR_TIMEOUT);
+                // drain barrier: completes when every MMA issued above has
+                // finished (the TMEM owner waits for it before freeing TMEM)
+                uint64_t* drain = reinterpret_cast<uint64_t*>(smem + UL::DRAIN);
+                if (any_mma) umma_commit(drain);
+                else mbar_arrive(drain);
             }
         }
         return;
@@ -785,10 +1041,24 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
     uint4* qk = qr + RG::QFRAG / 16;
     float* tsum = reinterpret_cast<float*>(smem + RG::TSUM);
     if (w == 0) {
-        build_q_frags<D>(p, s, hg, lane, qs);
+        if constexpr (UM) tmem_alloc(reinterpret_cast<uint32_t*>(smem + UL::TADDR), UL::TMEM_COLS);
+        build_q_frags<D, NH>(p, s, hg, lane, qs, smem + UL::QB, reinterpret_cast<float*>(smem + UL::ESC));
         if constexpr (VG == kTurbo) build_turbo_frags<D>(p, s, hg, lane, qr, qk, tsum);
+        if constexpr (UM) {
+            fence_proxy_async();   // B operand -> tensor-core reads
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(reinterpret_cast<uint64_t*>(smem + UL::QREADY));
+        }
     }
     named_sync(1, kConsumerThreads);
+    uint32_t tbase = 0;
+    float escale = 1.f;
+    if constexpr (UM) {
+        tc_fence_after();
+        tbase = *reinterpret_cast<volatile uint32_t*>(smem + UL::TADDR);
+        escale = *reinterpret_cast<volatile float*>(smem + UL::ESC);
+    }
     float cf[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float sum_r = 0.f, sum_k = 0.f;
     if constexpr (VG == kTurbo) {
@@ -813,10 +1083,43 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
             failed_at = k;
             break;
         }
-        const uint8_t* kbuf = smem + slot * RG::SLOT;
+        uint8_t* kbuf = smem + slot * RG::SLOT;
         const uint8_t* vbuf = kbuf + RG::VOFF;
         const int ntile = (cnt + kTile - 1) / kTile;
-        if (seg == 1) {
+        if (UM && seg == 1) {
+            uint64_t* mmab = reinterpret_cast<uint64_t*>(smem + UL::MMAB) + slot;
+            const uint32_t par = (k / kStages) & 1;
+            bool ok = true;
+            const int64_t row0 = srow0 + start;
+            constexpr int eb = 2 * RG::SEL;
+            const uint8_t* sd = kbuf + RG::SZOFF;
+            const uint16_t* sc = reinterpret_cast<const uint16_t*>(sd + ((row0 * eb) & 15));
+            const uint16_t* ze = reinterpret_cast<const uint16_t*>(sd + RG::RB0 + ((row0 * eb) & 15));
+            const uint32_t ta = tbase + ((uint32_t)(32 * w) << 16) + (uint32_t)(slot * 32);
+            if constexpr (UM) {
+                if (32 * w + 16 < cnt) {
+                    const int u0[2] = {32 * w, 32 * w + 16};
+                    uint32_t sz[2][4];
+                    load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
+                    load_sz<D, VG>(sc, ze, u0[1], cnt, lane, sz[1]);
+                    ok = far_tiles_um<D, VG, 2, NH>(kbuf, vbuf, u0, cnt, start, lane, w, ta, escale, mmab,
+                                                    par, sz, st);
+                } else if (32 * w < cnt) {
+                    const int u0[1] = {32 * w};
+                    uint32_t sz[1][4];
+                    load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
+                    ok = far_tiles_um<D, VG, 1, NH>(kbuf, vbuf, u0, cnt, start, lane, w, ta, escale, mmab,
+                                                    par, sz, st);
+                }
+            }
+            if (!ok) {
+                atomicExch(p.status, FKV_ERR_TIMEOUT);
+                failed_at = k;
+                break;
+            }
+            tc_fence_before();    // TMEM reads ordered before the slot release
+            fence_proxy_async();  // transpose writes ordered before the slot's next TMA fill
+        } else if (seg == 1) {
             // stage scalars: covering copies start at the 16-byte boundary below
             const int64_t row0 = srow0 + start;
             const uint8_t* sd = kbuf + RG::SZOFF;
@@ -862,8 +1165,9 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
     if (failed_at >= 0) {
         // the producer runs at most kStages ahead of the consumers: wait
         // (bounded) for the copies it may still have in flight, then leave
-        for (int k = failed_at; k < min(nstage, failed_at + kStages); ++k)
+        for (int k = failed_at; k < min(nstage, failed_at + kStages); ++k) {
             if (!mbar_wait(full + (k % kStages), (k / kStages) & 1)) break;
+        }
     }
 
     // ---- warp record -> shared memory (the ring is free once all consumers pass)
@@ -893,6 +1197,17 @@ __global__ void __launch_bounds__(kThreads, 3) decode_fp8_kernel(const DecodePar
         wr[R::O + (2 * c + 1) * D + d0 + 1] = st.o[i][3] + z1;
     }
     named_sync(1, kConsumerThreads);
+    if constexpr (UM) {
+        if (w == 0) {
+            // all consumer TMEM reads are done (barrier above); wait for the
+            // producer's drain commit so no MMA is in flight, then free TMEM
+            uint64_t* drain = reinterpret_cast<uint64_t*>(smem + UL::DRAIN);
+            for (int i = 0; i < 4; ++i)
+                if (mbar_wait(drain, 0)) break;
+            tc_fence_after();
+            tmem_dealloc(tbase, UL::TMEM_COLS);
+        }
+    }
 
     if (p.splits == 1) {
         merge_and_emit<D>(p, sh_rec, kConsumerWarps, R::SIZE, s, hg, false,
@@ -1007,7 +1322,9 @@ int num_sms() {
 
 // Resident CTAs per SM of one decode kernel instantiation (queried once per
 // device after opting it into its dynamic shared memory).
-int resident_ctas(void (*kern)(DecodeParams), int smem) {
+using KernelFn = void (*)(DecodeParams, CUtensorMap);
+
+int resident_ctas(KernelFn kern, int smem, int tmem_cols = 0) {
     static thread_local std::vector<std::pair<std::pair<int, const void*>, int>> cache;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 2;
@@ -1017,19 +1334,92 @@ int resident_ctas(void (*kern)(DecodeParams), int smem) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem) != cudaSuccess || n < 1)
         n = 2;
+    if (tmem_cols > 0) {
+        // the occupancy query answers 1 for kernels that allocate tensor
+        // memory; bound residency by registers, shared memory, threads and
+        // TMEM columns instead
+        cudaFuncAttributes fa{};
+        int sm_smem = 0, reserved = 0;
+        if (cudaFuncGetAttributes(&fa, (const void*)kern) == cudaSuccess &&
+            cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) == cudaSuccess) {
+            const int warps = (kThreads + 31) / 32;
+            const int regs_warp = ((fa.numRegs * 32 + 255) / 256) * 256;
+            const int by_regs = 65536 / std::max(1, regs_warp * warps);
+            const int by_smem = sm_smem / std::max(1, smem + (int)fa.sharedSizeBytes + reserved);
+            const int by_threads = 2048 / kThreads;
+            const int by_tmem = 512 / tmem_cols;
+            n = std::max(1, std::min(std::min(by_regs, by_smem), std::min(by_threads, by_tmem)));
+        }
+    }
     cache.push_back({{dev, (const void*)kern}, n});
     return n;
 }
 
-int resident_for(const FkvDecodeShape* sh, bool turbo) {
+// q heads per CTA on the tensor-core far path (0 = mma.sync path): fp8 K with
+// D = 128, a far tier, row indices inside the tensor map's int32 range, a GQA
+// group of at least two q heads.
+// FKV_QK_PATH=mma in the environment selects the mma.sync path.
+int um_heads(const FkvDecodeShape* sh, bool turbo) {
+    if (turbo || sh->D != 128 || sh->n_far <= 0) return 0;
+    if ((int64_t)sh->B * sh->Hk * sh->n_far >= ((int64_t)1 << 31) - 256) return 0;
+    if (sh->Hq / sh->Hk < 2) return 0;   // one q head: the mma.sync path is a little faster
+    const char* e = std::getenv("FKV_QK_PATH");
+    if (e != nullptr && std::strcmp(e, "mma") == 0) return 0;
+    return (sh->Hq / sh->Hk) <= 4 ? 4 : 8;
+}
+
+struct KernelPick {
+    KernelFn fn;
+    int smem;
+};
+
+KernelPick pick_kernel(const FkvDecodeShape* sh, bool turbo, int nh) {
     if (turbo)
-        return sh->D == 128 ? resident_ctas(decode_fp8_kernel<128, kTurbo>, Ring<128, kTurbo>::BYTES)
-                            : resident_ctas(decode_fp8_kernel<64, kTurbo>, Ring<64, kTurbo>::BYTES);
-    if (sh->D == 128)
-        return sh->v_group == 0 ? resident_ctas(decode_fp8_kernel<128, 0>, Ring<128, 0>::BYTES)
-                                : resident_ctas(decode_fp8_kernel<128, 32>, Ring<128, 32>::BYTES);
-    return sh->v_group == 0 ? resident_ctas(decode_fp8_kernel<64, 0>, Ring<64, 0>::BYTES)
-                            : resident_ctas(decode_fp8_kernel<64, 32>, Ring<64, 32>::BYTES);
+        return sh->D == 128 ? KernelPick{decode_fp8_kernel<128, kTurbo>, Ring<128, kTurbo>::BYTES}
+                            : KernelPick{decode_fp8_kernel<64, kTurbo>, Ring<64, kTurbo>::BYTES};
+    if (sh->D == 128) {
+        if (nh == 4)
+            return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<128, 0, 4>, UmLayout<128, 0>::BYTES}
+                                    : KernelPick{decode_fp8_kernel<128, 32, 4>, UmLayout<128, 32>::BYTES};
+        if (nh == 8)
+            return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<128, 0, 8>, UmLayout<128, 0>::BYTES}
+                                    : KernelPick{decode_fp8_kernel<128, 32, 8>, UmLayout<128, 32>::BYTES};
+        return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<128, 0>, Ring<128, 0>::BYTES}
+                                : KernelPick{decode_fp8_kernel<128, 32>, Ring<128, 32>::BYTES};
+    }
+    return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<64, 0>, Ring<64, 0>::BYTES}
+                            : KernelPick{decode_fp8_kernel<64, 32>, Ring<64, 32>::BYTES};
+}
+
+int resident_for(const FkvDecodeShape* sh, bool turbo, int nh = -1) {
+    if (nh < 0) nh = um_heads(sh, turbo);
+    const KernelPick k = pick_kernel(sh, turbo, nh);
+    return resident_ctas(k.fn, k.smem, nh > 0 ? (int)UmLayout<128, 0>::TMEM_COLS : 0);
+}
+
+// Tensor map of the far K codes as a (B*Hk*F, D) byte matrix read in boxes of
+// 128 rows with the 128-byte swizzle (the UMMA A-operand layout).  The driver
+// entry point is resolved once; false = unavailable (caller takes the
+// mma.sync path).
+bool far_k_tensor_map(const uint8_t* far_k, int64_t rows, int D, CUtensorMap* out) {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q{};
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    });
+    if (fn == nullptr) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)D};
+    const cuuint32_t box[2] = {(cuuint32_t)D, 128u};
+    const cuuint32_t es[2] = {1u, 1u};
+    return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(far_k), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 struct Plan {
@@ -1102,8 +1492,8 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 
 // Opt every kernel instantiation into its dynamic shared memory once per
 // device, then launch.
-int launch_kernel(void (*kern)(DecodeParams), int smem, dim3 grid, const DecodeParams& p,
-                  cudaStream_t st) {
+int launch_kernel(KernelFn kern, int smem, dim3 grid, const DecodeParams& p, cudaStream_t st,
+                  const CUtensorMap& kmap) {
     static thread_local std::vector<std::pair<int, const void*>> done;
     int dev = 0;
     FKV_CUDA_CHECK(cudaGetDevice(&dev));
@@ -1112,14 +1502,20 @@ int launch_kernel(void (*kern)(DecodeParams), int smem, dim3 grid, const DecodeP
         FKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         done.push_back(key);
     }
-    kern<<<grid, kThreads, smem, st>>>(p);
+    kern<<<grid, kThreads, smem, st>>>(p, kmap);
     FKV_LAUNCH_CHECK();
     return FKV_OK;
 }
 
 int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws_bytes,
            cudaStream_t st, bool turbo = false) {
-    const Plan pl = make_plan(sh, resident_for(sh, turbo));
+    int nh = um_heads(sh, turbo);
+    CUtensorMap kmap;
+    std::memset(&kmap, 0, sizeof(kmap));
+    if (nh > 0 && !far_k_tensor_map(p.far_k, (int64_t)sh->B * sh->Hk * sh->n_far, sh->D, &kmap))
+        nh = 0;
+    const KernelPick kp = pick_kernel(sh, turbo, nh);
+    const Plan pl = make_plan(sh, resident_ctas(kp.fn, kp.smem, nh > 0 ? (int)UmLayout<128, 0>::TMEM_COLS : 0));
     const size_t qoff = (pl.ticket_bytes + 255) & ~(size_t)255;
     const size_t front = turbo ? qoff + pl.qproj_bytes : pl.ticket_bytes;
     const size_t need = pl.rec_bytes + front + 256;
@@ -1143,21 +1539,13 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     if (turbo) {
         float* qproj = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + qoff);
         p.qproj = qproj;
-        if (sh->D == 128) {
+        if (sh->D == 128)
             turbo_qproj_kernel<128><<<sh->B * sh->Hq, 256, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj);
-            FKV_LAUNCH_CHECK();
-            return launch_kernel(decode_fp8_kernel<128, kTurbo>, Ring<128, kTurbo>::BYTES, grid, p, st);
-        }
-        turbo_qproj_kernel<64><<<sh->B * sh->Hq, 128, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj);
+        else
+            turbo_qproj_kernel<64><<<sh->B * sh->Hq, 128, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj);
         FKV_LAUNCH_CHECK();
-        return launch_kernel(decode_fp8_kernel<64, kTurbo>, Ring<64, kTurbo>::BYTES, grid, p, st);
     }
-    if (sh->D == 128) {
-        if (sh->v_group == 0) return launch_kernel(decode_fp8_kernel<128, 0>, Ring<128>::BYTES, grid, p, st);
-        return launch_kernel(decode_fp8_kernel<128, 32>, Ring<128, 32>::BYTES, grid, p, st);
-    }
-    if (sh->v_group == 0) return launch_kernel(decode_fp8_kernel<64, 0>, Ring<64>::BYTES, grid, p, st);
-    return launch_kernel(decode_fp8_kernel<64, 32>, Ring<64, 32>::BYTES, grid, p, st);
+    return launch_kernel(kp.fn, kp.smem, grid, p, st, kmap);
 }
 
 int fill_common(const FkvDecodeShape* sh, DecodeParams& p, const uint16_t* near_k,
@@ -1192,9 +1580,22 @@ size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s) {
     if (validate(s) != FKV_OK) return 0;
     // enough for either far-tier kind (their resident counts, hence split
     // counts, may differ)
+    // (and for either q.K path of the fp8 tier)
     const Plan a = make_plan(s, resident_for(s, false)), b = make_plan(s, resident_for(s, true));
-    const Plan& pl = a.rec_bytes >= b.rec_bytes ? a : b;
+    const Plan c = make_plan(s, resident_for(s, false, 0));
+    const Plan& ab = a.rec_bytes >= b.rec_bytes ? a : b;
+    const Plan& pl = ab.rec_bytes >= c.rec_bytes ? ab : c;
     return pl.rec_bytes + pl.ticket_bytes + 256 + ((pl.qproj_bytes + 255) & ~(size_t)255) + 256;
+}
+
+int fkv_decode_qk_path(const FkvDecodeShape* sh, const uint8_t* far_k) {
+    const int rc = validate(sh);
+    if (rc) return rc;
+    const int nh = um_heads(sh, false);
+    if (nh == 0) return 0;
+    FKV_REQUIRE(far_k != nullptr && aligned16(far_k), FKV_ERR_INVALID, "far_k NULL or misaligned");
+    CUtensorMap m;
+    return far_k_tensor_map(far_k, (int64_t)sh->B * sh->Hk * sh->n_far, sh->D, &m) ? nh : 0;
 }
 
 int fkv_decode_fp8(const FkvDecodeShape* sh, const uint16_t* near_k, const uint16_t* near_v,

@@ -158,6 +158,14 @@ int fkv_decode_fp8(const FkvDecodeShape* s, const uint16_t* near_k, const uint16
                    int32_t* flags, int32_t* tokens, void* workspace, size_t workspace_bytes,
                    void* stream);
 
+/* Which q.K path fkv_decode_fp8 / _partial / _noalloc take for this shape
+ * and far_k pointer (no counterpart in the reference, whose Metal kernel has
+ * one path): 4 or 8 = q heads per CTA on the 5th-generation tensor cores
+ * (tcgen05.mma on the E4M3 codes, scores in tensor memory; D = 128, G >= 2,
+ * a far tier), 0 = mma.sync after converting the codes, negative = invalid
+ * shape.  The environment variable FKV_QK_PATH=mma forces 0. */
+int fkv_decode_qk_path(const FkvDecodeShape* s, const uint8_t* far_k);
+
 /* TurboQuant far tier, scores directly on codes.  Replaces
  * TurboFoveatedHandle::operator() (csrc/foveated_attn.cpp:407-491) and kernel
  * foveated_2tier_turbo (csrc/kernels/foveated_attn.metal:559-767); the

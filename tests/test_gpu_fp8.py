@@ -84,12 +84,37 @@ DECODE_CASES = [
 ]
 
 
+@pytest.fixture(params=["auto", "mma"])
+def qk_path(request, monkeypatch):
+    """Run a decode test on the default q.K path (tcgen05 where the shape
+    allows it) and on the mma.sync path (FKV_QK_PATH=mma)."""
+    if request.param == "mma":
+        monkeypatch.setenv("FKV_QK_PATH", "mma")
+    else:
+        monkeypatch.delenv("FKV_QK_PATH", raising=False)
+    return request.param
+
+
+def _expect_path(lay, Hq, path):
+    """The library reports the q.K path the launch takes: tcgen05 (4 or 8 q
+    heads per CTA) for D = 128, G >= 2 and a far tier unless forced off."""
+    lib = _native.load()
+    sh = lay._fill_shape(Hq, lay.spike_margin)
+    got = lib.fkv_decode_qk_path(C.byref(sh), lay.far_k.data_ptr())
+    G = Hq // lay.near_k.shape[1]
+    want_tc = path == "auto" and lay.near_k.shape[-1] == 128 and G >= 2 and lay.n_far > 0
+    assert (got > 0) == want_tc, (got, path, G)
+    if want_tc:
+        assert got == (4 if G <= 4 else 8)
+
+
 @pytest.mark.parametrize("name,B,Hk,Hq,S,D,n_dec,kw,margin", DECODE_CASES)
-def test_decode_fp8_parity(name, B, Hk, Hq, S, D, n_dec, kw, margin):
+def test_decode_fp8_parity(name, B, Hk, Hq, S, D, n_dec, kw, margin, qk_path):
     w = numpy_workload(23, B, Hk, Hq, S, D, n_dec)
     cfg = TierConfig(spike_margin=margin, **kw)
     t = _tensors(w)
     lay = compress_layer(t["k"], t["v"], cfg)
+    _expect_path(lay, Hq, qk_path)
     for i in range(n_dec):
         lay.add_token(t["dec_k"][:, :, i:i + 1], t["dec_v"][:, :, i:i + 1])
     out, flags, tokens = lay.attend_fused_with_spikes(t["q"][:, :, None, :])
@@ -102,7 +127,7 @@ def test_decode_fp8_parity(name, B, Hk, Hq, S, D, n_dec, kw, margin):
 
 
 @pytest.mark.parametrize("splits", [1, 2, 3, 7, 40])
-def test_decode_split_counts_agree(splits):
+def test_decode_split_counts_agree(splits, qk_path):
     """Explicit split counts through the raw C ABI give the same answer."""
     w = numpy_workload(5, 2, 2, 8, 1500, 128, 9)
     t = _tensors(w)
