@@ -64,6 +64,7 @@ struct DecodeParams {
     const float* turbo_s;
     float qjl_coef;
     int B, Hq, Hk, G, HG, Np, F, n_dec, dec_stride, splits, chunk;
+    int near_w;           // cost units of an fp16 near / decode token (a far token is 1)
     float margin, qscale;
 };
 
@@ -195,7 +196,8 @@ struct Ring {
     static constexpr int QOFF = kStages * SLOT;                 // q (+ turbo q Pi^T, q S^T)
     static constexpr int TSUM = QOFF + (VG == kTurbo ? 3 : 1) * QFRAG;   // turbo row sums
     static constexpr int BAROFF = TSUM + (VG == kTurbo ? 64 : 0);        // mbarriers
-    static constexpr int BYTES = BAROFF + 2 * kStages * 8;
+    static constexpr int MERGEBAR = BAROFF + 2 * kStages * 8;          // 2 split-merge barriers
+    static constexpr int BYTES = MERGEBAR + 2 * 8;
 };
 
 // Extra shared memory of the tensor-core far path (placed after the ring's
@@ -574,24 +576,44 @@ __device__ __forceinline__ bool far_tiles_um(uint8_t* __restrict__ kbuf,
 // c covers dims 4(4j+c) .. 4(4j+c)+3 = code byte 4j+c of the token row.
 
 // q Pi^T and q S^T for every (b, q head), f32 (the reference does these two
-// products with host matmuls, foveated_attn.cpp:419-421)
+// products with host matmuls, foveated_attn.cpp:419-421).  A tiny GEMM
+// (B*Hq x D) . (D x 2D): each block stages kQpRows rows of [Pi; S] and kQpHeads
+// q vectors in shared memory with one round of 16-byte loads, then each
+// thread computes one (head, output) dot product.  Grid (2D / kQpRows,
+// ceil(B*Hq / kQpHeads)): wide, so the latency is a couple of load rounds.
+constexpr int kQpRows = 16, kQpHeads = 8, kQpThreads = kQpRows * kQpHeads;
+
 template <int D>
-__global__ void turbo_qproj_kernel(const uint16_t* __restrict__ q, const float* __restrict__ Pi,
-                                   const float* __restrict__ Sm, float* __restrict__ out) {
-    __shared__ float qv[D];
-    const int bh = blockIdx.x;
-    for (int i = threadIdx.x; i < D; i += blockDim.x)
-        qv[i] = __half2float(__ushort_as_half(q[(int64_t)bh * D + i]));
-    __syncthreads();
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int o = w; o < 2 * D; o += nw) {   // one warp per output, lanes along the row
-        const float* row = (o < D ? Pi + (int64_t)o * D : Sm + (int64_t)(o - D) * D);
-        float acc = 0.f;
-#pragma unroll
-        for (int i = lane; i < D; i += 32) acc = fmaf(qv[i], __ldg(row + i), acc);
-        for (int x = 16; x > 0; x >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, x);
-        if (lane == 0) out[(int64_t)bh * 2 * D + o] = acc;
+__global__ void __launch_bounds__(kQpThreads)
+    turbo_qproj_kernel(const uint16_t* __restrict__ q, const float* __restrict__ Pi,
+                       const float* __restrict__ Sm, float* __restrict__ out, int BH) {
+    __shared__ __align__(16) float mrow[kQpRows][D + 4];
+    __shared__ __align__(16) float qv[kQpHeads][D + 4];
+    const int o0 = blockIdx.x * kQpRows, h0 = blockIdx.y * kQpHeads;
+    const int tid = threadIdx.x;
+    for (int i = tid; i < kQpRows * D / 4; i += kQpThreads) {
+        const int r = i / (D / 4), c4 = i % (D / 4), o = o0 + r;
+        const float* src = (o < D ? Pi + (int64_t)o * D : Sm + (int64_t)(o - D) * D) + 4 * c4;
+        *reinterpret_cast<float4*>(&mrow[r][4 * c4]) = __ldg(reinterpret_cast<const float4*>(src));
     }
+    for (int i = tid; i < kQpHeads * D / 8; i += kQpThreads) {
+        const int j = i / (D / 8), c8 = i % (D / 8);
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (h0 + j < BH) w = __ldg(reinterpret_cast<const uint4*>(q + (int64_t)(h0 + j) * D) + c8);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 f = __half22float2(u32_as_h2(ws[e]));
+            qv[j][8 * c8 + 2 * e] = f.x;
+            qv[j][8 * c8 + 2 * e + 1] = f.y;
+        }
+    }
+    __syncthreads();
+    const int j = tid / kQpRows, r = tid % kQpRows;
+    float acc = 0.f;
+#pragma unroll 16
+    for (int i = 0; i < D; ++i) acc = fmaf(qv[j][i], mrow[r][i], acc);
+    if (h0 + j < BH) out[(int64_t)(h0 + j) * 2 * D + o0 + r] = acc;
 }
 
 // hi/lo fragments of q Pi^T and q S^T in the turbo permutation + per-head sums
@@ -757,53 +779,80 @@ __device__ __forceinline__ void turbo_tile(const uint8_t* __restrict__ sgn,
     }
 }
 
-// Merge `n` records (strided by `stride` floats; in shared memory for the
-// per-warp records, in the workspace for split records) and emit the output
-// or the sequence-split record.  The records' scalars are first staged in
-// shared memory with independent loads, per-head maxima / weights computed
-// once, then every thread accumulates its (head, d) outputs over the records
-// with many independent, coalesced loads in flight.
+// Merging `n` records of one (stream, head group): per-warp records of one
+// CTA (in shared memory) or the split records of all CTAs of the stream (in
+// the workspace), then the output or the sequence-split record is emitted.
+// merge_heads: the records' scalars are staged in shared memory with one
+// round of float4 loads, then 16 threads per head reduce the maxima, the
+// weights exp(m_k - M), the denominators and the spike trackers.  The o
+// vectors are then accumulated by every thread over its 8 (D = 128) or 4
+// (D = 64) contiguous outputs: straight from shared memory for the per-warp
+// records, through double-buffered bulk copies (TMA) of whole records for the
+// split records (bandwidth- instead of latency-bound for many splits).
 constexpr int kMaxSplits = 64;
+constexpr int kMergeScratch = (kMaxSplits * 40 + kMaxSplits * 8 + 8) * 4;   // bytes
 
-template <int D>
-__device__ __forceinline__ void merge_and_emit(const DecodeParams& p, const float* recs, int n,
-                                               int stride, int s, int hg, bool from_global,
-                                               float* __restrict__ scratch) {
+template <bool G>
+__device__ __forceinline__ float4 ld4(const float* a) {
+    if constexpr (G) return __ldcg(reinterpret_cast<const float4*>(a));
+    else return *reinterpret_cast<const float4*>(a);
+}
+
+template <int D, bool FROM_GLOBAL>
+__device__ __forceinline__ void merge_heads(const DecodeParams& p, const float* recs, int n,
+                                            int stride, int s, int hg, float* __restrict__ scratch) {
     using R = RecLayout<D>;
+    static_assert(kConsumerThreads == 128, "merge layout: 16 threads per head");
     const int tid = threadIdx.x;
     const int b = s / p.Hk, h = s % p.Hk;
     float* sc = scratch;                      // [n][40] record scalars
     float* wk = scratch + kMaxSplits * 40;    // [n][8] weights exp(m_k - M)
     float* hl = wk + kMaxSplits * 8;          // [8] L per head
-    for (int i = tid; i < n * 40; i += kConsumerThreads) {
-        const float* a = recs + (i / 40) * stride + (i % 40);
-        sc[i] = from_global ? __ldcg(a) : *a;
+    {
+        constexpr int PER = (kMaxSplits * 10 + kConsumerThreads - 1) / kConsumerThreads;
+        float4 t[PER];
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int i = tid + j * kConsumerThreads;
+            if (i < n * 10) t[j] = ld4<FROM_GLOBAL>(recs + (i / 10) * stride + (i % 10) * 4);
+        }
+#pragma unroll
+        for (int j = 0; j < PER; ++j) {
+            const int i = tid + j * kConsumerThreads;
+            if (i < n * 10) reinterpret_cast<float4*>(sc)[i] = t[j];
+        }
     }
     named_sync(1, kConsumerThreads);
-    if (tid < 8) {
-        const int head = tid;
-        const int g = hg * kHeadsPerTile + head;
-        float M = -INFINITY;
-        for (int k = 0; k < n; ++k) M = fmaxf(M, sc[k * 40 + R::M + head]);
-        float L = 0.f, mn = INFINITY, mf = -INFINITY;
-        int af = -1;
-        for (int k = 0; k < n; ++k) {
-            const float mk = sc[k * 40 + R::M + head];
-            const float wgt = (mk == -INFINITY) ? 0.f : exp2f((mk - M) * kLog2e);
-            wk[k * 8 + head] = wgt;
-            L = fmaf(wgt, sc[k * 40 + R::L + head], L);
-            mn = fminf(mn, sc[k * 40 + R::MN + head]);
-            argmax_merge(mf, af, sc[k * 40 + R::MF + head], __float_as_int(sc[k * 40 + R::AF + head]));
-        }
+    const int head = tid >> 4, sub = tid & 15;
+    float M = -INFINITY;
+    for (int k = sub; k < n; k += 16) M = fmaxf(M, sc[k * 40 + R::M + head]);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float L = 0.f, mn = INFINITY, mf = -INFINITY;
+    int af = -1;
+    for (int k = sub; k < n; k += 16) {
+        const float mk = sc[k * 40 + R::M + head];
+        const float wgt = (mk == -INFINITY) ? 0.f : exp2f((mk - M) * kLog2e);
+        wk[k * 8 + head] = wgt;
+        L = fmaf(wgt, sc[k * 40 + R::L + head], L);
+        mn = fminf(mn, sc[k * 40 + R::MN + head]);
+        argmax_merge(mf, af, sc[k * 40 + R::MF + head], __float_as_int(sc[k * 40 + R::AF + head]));
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+        L += __shfl_xor_sync(0xffffffffu, L, o);
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        const float mf2 = __shfl_xor_sync(0xffffffffu, mf, o);
+        const int af2 = __shfl_xor_sync(0xffffffffu, af, o);
+        argmax_merge(mf, af, mf2, af2);
+    }
+    const int g = hg * kHeadsPerTile + head;
+    if (sub == 0) {
         hl[head] = L;
         if (g < p.G) {
             const int64_t bh = (int64_t)b * p.Hq + (int64_t)h * p.G + g;
             if (p.part != nullptr) {
-                float* rec = p.part + bh * (D + 4);
-                rec[0] = M;
-                rec[1] = L;
-                rec[2] = mn;
-                rec[3] = mf;
+                *reinterpret_cast<float4*>(p.part + bh * (D + 4)) = make_float4(M, L, mn, mf);
                 p.part_arg[bh] = af >= 0 ? af + p.far_offset : -1;
             } else {
                 p.flags[bh] = (mf > mn + p.margin) ? 1 : 0;
@@ -812,34 +861,113 @@ __device__ __forceinline__ void merge_and_emit(const DecodeParams& p, const floa
         }
     }
     named_sync(1, kConsumerThreads);
-    constexpr int E = kHeadsPerTile * D / kConsumerThreads;   // outputs per thread
+}
+
+template <int D>
+__device__ __forceinline__ void merge_accumulate(float (&acc)[8 * D / kConsumerThreads],
+                                                 const float* rec, float wgt, int e0) {
+    using R = RecLayout<D>;
+    constexpr int E = 8 * D / kConsumerThreads;
+#pragma unroll
+    for (int j = 0; j < E / 4; ++j) {
+        const float4 v = *reinterpret_cast<const float4*>(rec + R::O + e0 + 4 * j);
+        acc[4 * j + 0] = fmaf(wgt, v.x, acc[4 * j + 0]);
+        acc[4 * j + 1] = fmaf(wgt, v.y, acc[4 * j + 1]);
+        acc[4 * j + 2] = fmaf(wgt, v.z, acc[4 * j + 2]);
+        acc[4 * j + 3] = fmaf(wgt, v.w, acc[4 * j + 3]);
+    }
+}
+
+// thread's E contiguous outputs -> out (fp16, divided by L) or the partial record
+template <int D>
+__device__ __forceinline__ void merge_emit(const DecodeParams& p, const float (&acc)[8 * D / kConsumerThreads],
+                                          int s, int hg, const float* __restrict__ scratch) {
+    constexpr int E = 8 * D / kConsumerThreads;
+    const float* hl = scratch + kMaxSplits * 40 + kMaxSplits * 8;
+    const int e0 = threadIdx.x * E, head = e0 / D, d0 = e0 % D;
+    const int g = hg * kHeadsPerTile + head;
+    if (g >= p.G) return;
+    const int b = s / p.Hk, h = s % p.Hk;
+    const int64_t bh = (int64_t)b * p.Hq + (int64_t)h * p.G + g;
+    if (p.part != nullptr) {
+        float* dst = p.part + bh * (D + 4) + 4 + d0;
+#pragma unroll
+        for (int j = 0; j < E / 4; ++j)
+            *reinterpret_cast<float4*>(dst + 4 * j) =
+                make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+    } else {
+        const float L = hl[head];
+        uint32_t hw[E / 2];
+#pragma unroll
+        for (int x = 0; x < E / 2; ++x)
+            hw[x] = pack_h2(L > 0.f ? acc[2 * x] / L : 0.f, L > 0.f ? acc[2 * x + 1] / L : 0.f);
+        uint16_t* dst = p.out + bh * D + d0;
+        if constexpr (E == 8) *reinterpret_cast<uint4*>(dst) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        else *reinterpret_cast<uint2*>(dst) = make_uint2(hw[0], hw[1]);
+    }
+}
+
+// the per-warp records of a single-split stream, in shared memory
+template <int D>
+__device__ __forceinline__ void merge_warps(const DecodeParams& p, const float* recs, int s, int hg,
+                                           float* __restrict__ scratch) {
+    using R = RecLayout<D>;
+    constexpr int E = 8 * D / kConsumerThreads;
+    merge_heads<D, false>(p, recs, kConsumerWarps, R::SIZE, s, hg, scratch);
+    const float* wk = scratch + kMaxSplits * 40;
+    const int e0 = threadIdx.x * E, head = e0 / D;
     float acc[E];
 #pragma unroll
     for (int x = 0; x < E; ++x) acc[x] = 0.f;
-#pragma unroll 4
-    for (int k = 0; k < n; ++k) {
-        const float* o = recs + k * stride + R::O;
 #pragma unroll
-        for (int x = 0; x < E; ++x) {
-            const int e = tid + x * kConsumerThreads;
-            const float v = from_global ? __ldcg(o + e) : o[e];
-            acc[x] = fmaf(wk[k * 8 + e / D], v, acc[x]);
-        }
+    for (int k = 0; k < kConsumerWarps; ++k) merge_accumulate<D>(acc, recs + k * R::SIZE, wk[k * 8 + head], e0);
+    merge_emit<D>(p, acc, s, hg, scratch);
+}
+
+// the split records of one stream in the workspace (run by the stream's last
+// CTA): scalars by loads, o vectors through bulk copies of a few records at a
+// time into two shared-memory buffers (mbar[0], mbar[1]) behind the scratch
+template <int D>
+__device__ __forceinline__ void merge_splits(const DecodeParams& p, const float* base, int n, int s,
+                                            int hg, uint8_t* smem, uint64_t* mbar) {
+    using R = RecLayout<D>;
+    constexpr int E = 8 * D / kConsumerThreads;
+    constexpr int RB = R::SIZE * 4;                      // record bytes (multiple of 16)
+    constexpr int BUF0 = (kMergeScratch + 127) & ~127;
+    // records per bulk copy: two buffers in the ring behind the scratch
+    constexpr int kMergeBatch = (kStages * Ring<D>::SLOT - BUF0) / (2 * RB);
+    static_assert(RB % 16 == 0 && kMergeBatch >= 2, "merge buffers must fit in the ring");
+    float* scratch = reinterpret_cast<float*>(smem);
+    const int nb = (n + kMergeBatch - 1) / kMergeBatch;
+    auto issue = [&](int bi) {
+        const int cnt = min(kMergeBatch, n - bi * kMergeBatch);
+        uint8_t* dst = smem + BUF0 + (bi & 1) * kMergeBatch * RB;
+        bulk_g2s(dst, base + (int64_t)bi * kMergeBatch * R::SIZE, (uint32_t)(cnt * RB), mbar + (bi & 1));
+        mbar_arrive_expect_tx(mbar + (bi & 1), (uint32_t)(cnt * RB));
+    };
+    if (threadIdx.x == 0) {
+        // records written by other CTAs (generic proxy, ordered by the ticket)
+        // and this CTA's earlier shared-memory use, before async-proxy copies
+        asm volatile("fence.proxy.async.global;\n" ::: "memory");
+        fence_proxy_async();
+        for (int bi = 0; bi < min(nb, 2); ++bi) issue(bi);
     }
+    merge_heads<D, true>(p, base, n, R::SIZE, s, hg, scratch);
+    const float* wk = scratch + kMaxSplits * 40;
+    const int e0 = threadIdx.x * E, head = e0 / D;
+    float acc[E];
 #pragma unroll
-    for (int x = 0; x < E; ++x) {
-        const int e = tid + x * kConsumerThreads;
-        const int head = e / D, d = e % D;
-        const int g = hg * kHeadsPerTile + head;
-        if (g >= p.G) continue;
-        const int64_t bh = (int64_t)b * p.Hq + (int64_t)h * p.G + g;
-        if (p.part != nullptr) {
-            p.part[bh * (D + 4) + 4 + d] = acc[x];
-        } else {
-            const float L = hl[head];
-            p.out[bh * D + d] = __half_as_ushort(__float2half_rn(L > 0.f ? acc[x] / L : 0.f));
-        }
+    for (int x = 0; x < E; ++x) acc[x] = 0.f;
+    for (int bi = 0; bi < nb; ++bi) {
+        if (!mbar_wait(mbar + (bi & 1), (bi >> 1) & 1)) atomicExch(p.status, FKV_ERR_TIMEOUT);
+        const float* buf = reinterpret_cast<const float*>(smem + BUF0 + (bi & 1) * kMergeBatch * RB);
+        const int cnt = min(kMergeBatch, n - bi * kMergeBatch);
+        for (int u = 0; u < cnt; ++u)
+            merge_accumulate<D>(acc, buf + u * R::SIZE, wk[(bi * kMergeBatch + u) * 8 + head], e0);
+        named_sync(1, kConsumerThreads);   // buffer (bi & 1) is free again
+        if (threadIdx.x == 0 && bi + 2 < nb) issue(bi + 2);
     }
+    merge_emit<D>(p, acc, s, hg, scratch);
 }
 
 // NH = 0: far-tier q.K on mma.sync after converting the codes; NH = 4 or 8:
@@ -868,6 +996,8 @@ __global__ void __launch_bounds__(kThreads, 3)
             mbar_init(full + i, 1);
             mbar_init(empty + i, kConsumerWarps);
         }
+        mbar_init(reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR), 1);
+        mbar_init(reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR) + 1, 1);
         if constexpr (UM) {
             for (int i = 0; i < kStages; ++i) mbar_init(reinterpret_cast<uint64_t*>(smem + UL::MMAB) + i, 1);
             mbar_init(reinterpret_cast<uint64_t*>(smem + UL::QREADY), 1);
@@ -876,14 +1006,16 @@ __global__ void __launch_bounds__(kThreads, 3)
         fence_mbar_init();
     }
     // segments of this split's chunk [t0, t1) of [near valid | far | decode]
-    // splits are even in cost units (an fp16 near / decode token weighs 2, a
-    // compressed far token 1); map this split's cost range back to tokens
+    // splits are even in cost units (an fp16 near / decode token weighs
+    // near_w, a compressed far token 1); map this split's cost range back to
+    // tokens
+    const int64_t nw = p.near_w;
     auto to_tok = [&](int64_t cu) -> int {
-        if (cu <= 2 * (int64_t)p.Np) return (int)(cu / 2);
-        if (cu <= 2 * (int64_t)p.Np + p.F) return (int)(cu - p.Np);
-        return p.Np + p.F + (int)((cu - 2 * (int64_t)p.Np - p.F) / 2);
+        if (cu <= nw * p.Np) return (int)(cu / nw);
+        if (cu <= nw * p.Np + p.F) return (int)(cu - nw * p.Np) + p.Np;
+        return p.Np + p.F + (int)((cu - nw * p.Np - p.F) / nw);
     };
-    const int64_t total_cost = 2 * (int64_t)p.Np + p.F + 2 * (int64_t)p.n_dec;
+    const int64_t total_cost = nw * p.Np + p.F + nw * p.n_dec;
     const int t0 = to_tok(min((int64_t)split * p.chunk, total_cost));
     const int t1 = to_tok(min((int64_t)(split + 1) * p.chunk, total_cost));
     const int nv = min(max(__ldg(p.near_valid + s), 0), p.Np);
@@ -1210,50 +1342,49 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
 
     if (p.splits == 1) {
-        merge_and_emit<D>(p, sh_rec, kConsumerWarps, R::SIZE, s, hg, false,
-                          sh_rec + kConsumerWarps * R::SIZE);
+        merge_warps<D>(p, sh_rec, s, hg, sh_rec + kConsumerWarps * R::SIZE);
         return;
     }
 
     // ---- CTA record -> workspace, then the last CTA of this stream merges
     const int64_t slotrec = ((int64_t)s * p.HG + hg) * p.splits + split;
     float* gr = p.ws + slotrec * R::SIZE;
-    for (int e = threadIdx.x; e < 8 * D + 8; e += kConsumerThreads) {
-        if (e < 8 * D) {
-            const int head = e / D;
-            float M = -INFINITY;
+    float* cw = sh_rec + kConsumerWarps * R::SIZE;   // [warp][head] weights exp(m_w - M)
+    if (threadIdx.x < kHeadsPerTile) {
+        const int head = threadIdx.x;
+        float M = -INFINITY, L = 0.f, mn = INFINITY, mf = -INFINITY;
+        int af = -1;
 #pragma unroll
-            for (int k = 0; k < kConsumerWarps; ++k) M = fmaxf(M, sh_rec[k * R::SIZE + R::M + head]);
-            float acc = 0.f;
-            if (M != -INFINITY) {
+        for (int k = 0; k < kConsumerWarps; ++k) M = fmaxf(M, sh_rec[k * R::SIZE + R::M + head]);
 #pragma unroll
-                for (int k = 0; k < kConsumerWarps; ++k) {
-                    const float mk = sh_rec[k * R::SIZE + R::M + head];
-                    if (mk != -INFINITY)
-                        acc = fmaf(exp2f((mk - M) * kLog2e), sh_rec[k * R::SIZE + R::O + e], acc);
-                }
-            }
-            gr[R::O + e] = acc;
-        } else {
-            const int head = e - 8 * D;
-            float M = -INFINITY, L = 0.f, mn = INFINITY, mf = -INFINITY;
-            int af = -1;
-#pragma unroll
-            for (int k = 0; k < kConsumerWarps; ++k) M = fmaxf(M, sh_rec[k * R::SIZE + R::M + head]);
-#pragma unroll
-            for (int k = 0; k < kConsumerWarps; ++k) {
-                const float* q = sh_rec + k * R::SIZE;
-                if (q[R::M + head] != -INFINITY)
-                    L = fmaf(exp2f((q[R::M + head] - M) * kLog2e), q[R::L + head], L);
-                mn = fminf(mn, q[R::MN + head]);
-                argmax_merge(mf, af, q[R::MF + head], __float_as_int(q[R::AF + head]));
-            }
-            gr[R::M + head] = M;
-            gr[R::L + head] = L;
-            gr[R::MN + head] = mn;
-            gr[R::MF + head] = mf;
-            gr[R::AF + head] = __int_as_float(af);
+        for (int k = 0; k < kConsumerWarps; ++k) {
+            const float* q = sh_rec + k * R::SIZE;
+            const float wgt = (q[R::M + head] == -INFINITY) ? 0.f : exp2f((q[R::M + head] - M) * kLog2e);
+            cw[k * kHeadsPerTile + head] = wgt;
+            L = fmaf(wgt, q[R::L + head], L);
+            mn = fminf(mn, q[R::MN + head]);
+            argmax_merge(mf, af, q[R::MF + head], __float_as_int(q[R::AF + head]));
         }
+        gr[R::M + head] = M;
+        gr[R::L + head] = L;
+        gr[R::MN + head] = mn;
+        gr[R::MF + head] = mf;
+        gr[R::AF + head] = __int_as_float(af);
+    }
+    named_sync(1, kConsumerThreads);
+    for (int e = 4 * threadIdx.x; e < kHeadsPerTile * D; e += 4 * kConsumerThreads) {
+        const int head = e / D;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < kConsumerWarps; ++k) {
+            const float wgt = cw[k * kHeadsPerTile + head];
+            const float4 o = *reinterpret_cast<const float4*>(sh_rec + k * R::SIZE + R::O + e);
+            acc.x = fmaf(wgt, o.x, acc.x);
+            acc.y = fmaf(wgt, o.y, acc.y);
+            acc.z = fmaf(wgt, o.z, acc.z);
+            acc.w = fmaf(wgt, o.w, acc.w);
+        }
+        *reinterpret_cast<float4*>(gr + R::O + e) = acc;
     }
     __threadfence();
     named_sync(1, kConsumerThreads);
@@ -1267,7 +1398,7 @@ __global__ void __launch_bounds__(kThreads, 3)
     if (!sh_last) return;
     __threadfence();
     const float* base = p.ws + ((int64_t)s * p.HG + hg) * p.splits * R::SIZE;
-    merge_and_emit<D>(p, base, p.splits, R::SIZE, s, hg, true, sh_rec);
+    merge_splits<D>(p, base, p.splits, s, hg, smem, reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR));
 }
 
 template <int D>
@@ -1426,22 +1557,27 @@ struct Plan {
     int HG, splits, chunk;
     size_t rec_bytes, ticket_bytes;
     size_t qproj_bytes;   // turbo only: (B*Hq, 2D) f32 after the counters
+    int near_w;
 };
 
-Plan make_plan(const FkvDecodeShape* sh, int resident) {
+// Cost model (measured on B200): an fp8 far token is the unit and an fp16
+// near / decode token costs 2; a TurboQuant far token costs about as much as
+// an fp16 one, so there both weigh 1 and the fixed costs shrink accordingly.
+Plan make_plan(const FkvDecodeShape* sh, int resident, bool turbo = false) {
     Plan pl{};
     const int G = sh->Hq / sh->Hk;
     pl.HG = (G + kHeadsPerTile - 1) / kHeadsPerTile;
-    // work of a (b, kv head) stream in cost units: fp16 near / decode tokens
-    // take about twice as long as compressed far tokens
-    const int64_t T = 2 * (int64_t)sh->n_near_alloc + sh->n_far + 2 * (int64_t)sh->n_dec;
+    pl.near_w = turbo ? 1 : 2;
+    const double fixed = turbo ? 300.0 : 512.0, per_split = turbo ? 4.0 : 8.0;
+    // work of a (b, kv head) stream in cost units
+    const int64_t T = pl.near_w * ((int64_t)sh->n_near_alloc + sh->n_dec) + sh->n_far;
     const int64_t streams = (int64_t)sh->B * sh->Hk * pl.HG;
     int splits = sh->num_splits;
     if (splits <= 0) {
         // Pick the split count minimising (waves of resident CTAs) x (chunk
-        // length + a fixed per-CTA cost of ~512 tokens: q fragments, pipeline
-        // fill, record write) + ~48 tokens per split record the last CTA of a
-        // stream merges.  Balances wave quantisation against CTA overhead:
+        // length + a fixed per-CTA cost: launch, q fragments, pipeline fill,
+        // record write) + a small cost per split record the last CTA of a
+        // stream merges (bulk copies).  Balances wave quantisation against CTA overhead:
         // few long CTAs for a handful of (b, kv head) streams, a few splits
         // for large batches.
         const int64_t slots = (int64_t)num_sms() * std::max(resident, 1);
@@ -1451,7 +1587,7 @@ Plan make_plan(const FkvDecodeShape* sh, int resident) {
             const int64_t chunk_tok = (T + sp - 1) / sp;
             if (sp > 1 && chunk_tok < 256) break;
             const int64_t waves = (streams * sp + slots - 1) / slots;
-            const double cost = (double)waves * (double)(chunk_tok + 512) + 48.0 * sp;
+            const double cost = (double)waves * ((double)chunk_tok + fixed) + per_split * sp;
             if (cost < best * 0.999) {
                 best = cost;
                 splits = sp;
@@ -1515,7 +1651,8 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     if (nh > 0 && !far_k_tensor_map(p.far_k, (int64_t)sh->B * sh->Hk * sh->n_far, sh->D, &kmap))
         nh = 0;
     const KernelPick kp = pick_kernel(sh, turbo, nh);
-    const Plan pl = make_plan(sh, resident_ctas(kp.fn, kp.smem, nh > 0 ? (int)UmLayout<128, 0>::TMEM_COLS : 0));
+    const Plan pl =
+        make_plan(sh, resident_ctas(kp.fn, kp.smem, nh > 0 ? (int)UmLayout<128, 0>::TMEM_COLS : 0), turbo);
     const size_t qoff = (pl.ticket_bytes + 255) & ~(size_t)255;
     const size_t front = turbo ? qoff + pl.qproj_bytes : pl.ticket_bytes;
     const size_t need = pl.rec_bytes + front + 256;
@@ -1524,7 +1661,7 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     FKV_REQUIRE(aligned16(workspace), FKV_ERR_INVALID, "workspace must be 16-byte aligned");
     p.B = sh->B; p.Hq = sh->Hq; p.Hk = sh->Hk; p.G = sh->Hq / sh->Hk; p.HG = pl.HG;
     p.Np = sh->n_near_alloc; p.F = sh->n_far; p.n_dec = sh->n_dec; p.dec_stride = sh->dec_stride;
-    p.splits = pl.splits; p.chunk = pl.chunk; p.margin = sh->spike_margin;
+    p.splits = pl.splits; p.chunk = pl.chunk; p.near_w = pl.near_w; p.margin = sh->spike_margin;
     p.qscale = (float)(1.0 / sqrt((double)sh->D));   // same f32 constant as the host oracle
     // split counters at the front, split records at the back: a workspace
     // shared by calls of different shapes keeps every counter at zero as long
@@ -1539,10 +1676,14 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     if (turbo) {
         float* qproj = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + qoff);
         p.qproj = qproj;
+        const int BH = sh->B * sh->Hq;
+        FKV_REQUIRE((BH + kQpHeads - 1) / kQpHeads <= 65535, FKV_ERR_UNSUPPORTED,
+                    "B*Hq=%d exceeds the q-projection grid limit", BH);
+        const dim3 qg(2 * sh->D / kQpRows, (BH + kQpHeads - 1) / kQpHeads);
         if (sh->D == 128)
-            turbo_qproj_kernel<128><<<sh->B * sh->Hq, 256, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj);
+            turbo_qproj_kernel<128><<<qg, kQpThreads, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj, BH);
         else
-            turbo_qproj_kernel<64><<<sh->B * sh->Hq, 128, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj);
+            turbo_qproj_kernel<64><<<qg, kQpThreads, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj, BH);
         FKV_LAUNCH_CHECK();
     }
     return launch_kernel(kp.fn, kp.smem, grid, p, st, kmap);
@@ -1581,7 +1722,7 @@ size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s) {
     // enough for either far-tier kind (their resident counts, hence split
     // counts, may differ)
     // (and for either q.K path of the fp8 tier)
-    const Plan a = make_plan(s, resident_for(s, false)), b = make_plan(s, resident_for(s, true));
+    const Plan a = make_plan(s, resident_for(s, false)), b = make_plan(s, resident_for(s, true), true);
     const Plan c = make_plan(s, resident_for(s, false, 0));
     const Plan& ab = a.rec_bytes >= b.rec_bytes ? a : b;
     const Plan& pl = ab.rec_bytes >= c.rec_bytes ? ab : c;
@@ -1610,6 +1751,7 @@ int fkv_decode_fp8(const FkvDecodeShape* sh, const uint16_t* near_k, const uint1
                          dec_k, dec_v);
     if (rc) return rc;
     FKV_REQUIRE(out && flags && tokens, FKV_ERR_INVALID, "outputs are NULL");
+    FKV_REQUIRE(aligned16(out), FKV_ERR_INVALID, "out must be 16-byte aligned");
     p.out = out; p.flags = flags; p.tokens = tokens;
     return launch(sh, p, workspace, workspace_bytes, (cudaStream_t)stream);
 }
@@ -1640,6 +1782,7 @@ int fkv_decode_turbo(const FkvDecodeShape* sh, const uint16_t* near_k, const uin
     p.k_signs = k_signs; p.k_norm = k_norm; p.k_gamma = k_gamma; p.centroids = centroids;
     p.turbo_pi = Pi; p.turbo_s = Smat; p.qjl_coef = sh->qjl_coef;
     p.q = q; p.dec_k = dec_k; p.dec_v = dec_v;
+    FKV_REQUIRE(aligned16(out), FKV_ERR_INVALID, "out must be 16-byte aligned");
     p.out = out; p.flags = flags; p.tokens = tokens;
     return launch(sh, p, workspace, workspace_bytes, (cudaStream_t)stream, true);
 }
@@ -1657,6 +1800,7 @@ int fkv_decode_fp8_partial(const FkvDecodeShape* sh, const uint16_t* near_k,
                          dec_k, dec_v);
     if (rc) return rc;
     FKV_REQUIRE(part && part_arg, FKV_ERR_INVALID, "partial outputs are NULL");
+    FKV_REQUIRE(aligned16(part), FKV_ERR_INVALID, "part must be 16-byte aligned");
     p.part = part; p.part_arg = part_arg; p.far_offset = far_index_offset;
     return launch(sh, p, workspace, workspace_bytes, (cudaStream_t)stream);
 }

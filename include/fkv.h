@@ -150,7 +150,8 @@ size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s);
  *   near_k/near_v (B,Hk,Np,D) fp16; near_valid (B,Hk) int32
  *   far_k (B,Hk,F,D) u8; far_v (B,Hk,F,D/2) u8; v_scale/v_zero as compress
  *   q (B,Hq,D) fp16; dec_k/dec_v (B,Hk,dec_stride,D) fp16 (NULL if n_dec==0)
- *   out (B,Hq,D) fp16; flags (B,Hq) int32; tokens (B,Hq) int32 far-local or -1 */
+ *   out (B,Hq,D) fp16, 16-byte aligned; flags (B,Hq) int32; tokens (B,Hq)
+ *   int32 far-local or -1 */
 int fkv_decode_fp8(const FkvDecodeShape* s, const uint16_t* near_k, const uint16_t* near_v,
                    const int32_t* near_valid, const uint8_t* far_k, const uint8_t* far_v,
                    const uint16_t* v_scale, const uint16_t* v_zero, const uint16_t* q,
@@ -200,7 +201,7 @@ int fkv_decode_fp8_noalloc(const FkvDecodeShape* s, const uint16_t* near_k,
 /* Sequence-split variant (no reference counterpart; the reference has no
  * multi-device code): same attention over this shard's tiers, but instead of
  * the final output writes one partial record per (b, q head):
- *   part (B*Hq, D+4) f32 = [m, l, min_near, max_far, o[0..D)] with o
+ *   part (B*Hq, D+4) f32 (16-byte aligned) = [m, l, min_near, max_far, o[0..D)] with o
  *   unnormalised (sum of exp(s-m) v);  part_arg (B*Hq) int32 = argmax far
  *   index + far_index_offset (global far index), or -1. */
 int fkv_decode_fp8_partial(const FkvDecodeShape* s, const uint16_t* near_k,
