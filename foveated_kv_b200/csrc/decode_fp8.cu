@@ -70,6 +70,17 @@ struct DecodeParams {
 
 constexpr int kTurbo = -1;   // VG value selecting the TurboQuant far tier
 
+// Tensor maps of the tier tensors read with tiled TMA copies in the 128-byte
+// swizzle: far K codes as (B*Hk*F, D) bytes in 128-row boxes (tensor-core
+// path only), near tier and decode buffer as (rows, D) fp16 in boxes of 64
+// rows x 64 halves (one box per 128-byte half row).
+struct TMaps {
+    CUtensorMap far_k;
+    CUtensorMap near_k, near_v;
+    CUtensorMap dec_k, dec_v;
+};
+constexpr int kHalfBox = 64 * 128;   // bytes of one 64-row x 128-byte fp16 box
+
 // record = merged state of up to 8 q heads over a token range
 template <int D>
 struct RecLayout {
@@ -197,7 +208,7 @@ struct Ring {
     static constexpr int TSUM = QOFF + (VG == kTurbo ? 3 : 1) * QFRAG;   // turbo row sums
     static constexpr int BAROFF = TSUM + (VG == kTurbo ? 64 : 0);        // mbarriers
     static constexpr int MERGEBAR = BAROFF + 2 * kStages * 8;          // 2 split-merge barriers
-    static constexpr int BYTES = MERGEBAR + 2 * 8;
+    static constexpr int BYTES = MERGEBAR + 2 * 8;   // (+1024 at launch: base alignment slack)
 };
 
 // Extra shared memory of the tensor-core far path (placed after the ring's
@@ -263,6 +274,14 @@ __device__ __forceinline__ void stage_at(const Segs& sg, int k, int& seg, int& s
 }
 
 // ---- one 16-token tile of an fp16 stage (near tier or decode buffer) ----
+// The stage holds each of K and V as 128-byte half rows of 64 tokens in the
+// 128-byte swizzle: 16-byte chunk j of token u's 2D-byte row sits at half
+// j / 8, chunk (j % 8) ^ (u % 8).  The B-fragment reads of K (lane (r, c):
+// token r, bytes [c*D/2, (c+1)*D/2)) are then spread over all banks.
+__device__ __forceinline__ int sw128_off(int u, int j) {
+    return (j >> 3) * kHalfBox + u * 128 + (((j & 7) ^ (u & 7)) << 4);
+}
+
 template <int D>
 __device__ __forceinline__ void fp16_tile(const uint8_t* __restrict__ kbuf,
                                           const uint8_t* __restrict__ vbuf, int u0, int cnt,
@@ -275,10 +294,9 @@ __device__ __forceinline__ void fp16_tile(const uint8_t* __restrict__ kbuf,
 #pragma unroll
     for (int n = 0; n < 2; ++n) {
         const int u = u0 + 8 * n + r;
-        const uint4* src = reinterpret_cast<const uint4*>(kbuf + u * (2 * D) + c * (D / 2));
 #pragma unroll
         for (int x = 0; x < KW / 4; ++x) {
-            const uint4 w = src[x];
+            const uint4 w = *reinterpret_cast<const uint4*>(kbuf + sw128_off(u, c * (KW / 4) + x));
             kr[n][4 * x] = w.x; kr[n][4 * x + 1] = w.y; kr[n][4 * x + 2] = w.z; kr[n][4 * x + 3] = w.w;
         }
     }
@@ -287,10 +305,10 @@ __device__ __forceinline__ void fp16_tile(const uint8_t* __restrict__ kbuf,
     for (int e = 0; e < 4; ++e) {
         const int u = u0 + (e >> 1) * 8 + 2 * c + (e & 1);
         const bool ok = u < cnt;
-        const uint4* src = reinterpret_cast<const uint4*>(vbuf + u * (2 * D) + r * (D / 4));
 #pragma unroll
         for (int x = 0; x < VW / 4; ++x) {
-            const uint4 w = ok ? src[x] : make_uint4(0, 0, 0, 0);
+            const uint4 w = ok ? *reinterpret_cast<const uint4*>(vbuf + sw128_off(u, r * (VW / 4) + x))
+                               : make_uint4(0, 0, 0, 0);
             vr[e][4 * x] = w.x; vr[e][4 * x + 1] = w.y; vr[e][4 * x + 2] = w.z; vr[e][4 * x + 3] = w.w;
         }
     }
@@ -971,19 +989,19 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, const float*
 }
 
 // NH = 0: far-tier q.K on mma.sync after converting the codes; NH = 4 or 8:
-// far-tier q.K on tcgen05 (NH q heads per CTA, D = 128, E4M3 K; kmap is the
-// tensor map of far_k as (B*Hk*F rows, D bytes), unused when NH = 0).
+// far-tier q.K on tcgen05 (NH q heads per CTA, D = 128, E4M3 K; maps.far_k
+// is used only then).
 template <int D, int VG, int NH = 0>
 __global__ void __launch_bounds__(kThreads, 3)
-    decode_fp8_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap) {
+    decode_fp8_kernel(const DecodeParams p, const __grid_constant__ TMaps maps) {
     using R = RecLayout<D>;
     using RG = Ring<D, VG>;
     using UL = UmLayout<D, VG>;
     constexpr bool UM = NH > 0;
     static_assert(!UM || (D == 128 && VG != kTurbo), "tensor-core far path: fp8 K, D = 128");
     extern __shared__ __align__(128) uint8_t smem_raw[];
-    uint8_t* smem = smem_raw;
-    if constexpr (UM) smem += (1024u - (smem_u32(smem_raw) & 1023u)) & 1023u;
+    // 1024-byte aligned base: the swizzled TMA boxes and UMMA operands
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + RG::BAROFF);
     uint4* qs = reinterpret_cast<uint4*>(smem + RG::QOFF);
     uint64_t* empty = full + kStages;
@@ -1033,12 +1051,8 @@ __global__ void __launch_bounds__(kThreads, 3)
     if (w == kConsumerWarps) {
         // ---------------- producer warp: one elected lane issues bulk copies
         if (lane == 0) {
-            const uint8_t* nk = reinterpret_cast<const uint8_t*>(p.near_k) + (int64_t)s * p.Np * D * 2;
-            const uint8_t* nvp = reinterpret_cast<const uint8_t*>(p.near_v) + (int64_t)s * p.Np * D * 2;
             const uint8_t* fk = p.far_k + (int64_t)s * p.F * D;
             const uint8_t* fv = p.far_v + (int64_t)s * p.F * (D / 2);
-            const uint8_t* dk = reinterpret_cast<const uint8_t*>(p.dec_k) + (int64_t)s * p.dec_stride * D * 2;
-            const uint8_t* dv = reinterpret_cast<const uint8_t*>(p.dec_v) + (int64_t)s * p.dec_stride * D * 2;
             // copies of stage k into slot k % kStages, completing on full[slot]
             auto issue = [&](int k) {
                 const int slot = k % kStages;
@@ -1062,13 +1076,23 @@ __global__ void __launch_bounds__(kThreads, 3)
                     kb = cnt * D;
                     vb = cnt * (D / 2);
                 } else {
-                    ks = (seg == 0 ? nk : dk) + (int64_t)start * D * 2;
-                    vs = (seg == 0 ? nvp : dv) + (int64_t)start * D * 2;
-                    kb = vb = cnt * D * 2;
+                    ks = vs = nullptr;                                     // tensor-map copies below
+                    kb = vb = RG::NEAR_TOK * D * 2;                        // whole boxes
                 }
-                if (seg == 1 && UM) tma_load_2d(dst, &kmap, 0, (int)((int64_t)s * p.F + start), full + slot);
-                else bulk_g2s(dst, ks, kb, full + slot);
-                bulk_g2s(dst + RG::VOFF, vs, vb, full + slot);
+                if (seg != 1) {
+                    const CUtensorMap* mk = seg == 0 ? &maps.near_k : &maps.dec_k;
+                    const CUtensorMap* mv = seg == 0 ? &maps.near_v : &maps.dec_v;
+                    const int row = (int)((int64_t)s * (seg == 0 ? p.Np : p.dec_stride) + start);
+#pragma unroll
+                    for (int hh = 0; hh < 2 * D / 128; ++hh) {
+                        tma_load_2d(dst + hh * kHalfBox, mk, 64 * hh, row, full + slot);
+                        tma_load_2d(dst + RG::VOFF + hh * kHalfBox, mv, 64 * hh, row, full + slot);
+                    }
+                } else {
+                    if (UM) tma_load_2d(dst, &maps.far_k, 0, (int)((int64_t)s * p.F + start), full + slot);
+                    else bulk_g2s(dst, ks, kb, full + slot);
+                    bulk_g2s(dst + RG::VOFF, vs, vb, full + slot);
+                }
                 uint32_t tx = kb + vb;
                 if (seg == 1) {
                     const int64_t row0 = (int64_t)s * p.F + start, nrows = (int64_t)p.B * p.Hk * p.F;
@@ -1453,7 +1477,7 @@ int num_sms() {
 
 // Resident CTAs per SM of one decode kernel instantiation (queried once per
 // device after opting it into its dynamic shared memory).
-using KernelFn = void (*)(DecodeParams, CUtensorMap);
+using KernelFn = void (*)(DecodeParams, TMaps);
 
 int resident_ctas(KernelFn kern, int smem, int tmem_cols = 0) {
     static thread_local std::vector<std::pair<std::pair<int, const void*>, int>> cache;
@@ -1507,8 +1531,8 @@ struct KernelPick {
 
 KernelPick pick_kernel(const FkvDecodeShape* sh, bool turbo, int nh) {
     if (turbo)
-        return sh->D == 128 ? KernelPick{decode_fp8_kernel<128, kTurbo>, Ring<128, kTurbo>::BYTES}
-                            : KernelPick{decode_fp8_kernel<64, kTurbo>, Ring<64, kTurbo>::BYTES};
+        return sh->D == 128 ? KernelPick{decode_fp8_kernel<128, kTurbo>, Ring<128, kTurbo>::BYTES + 1024}
+                            : KernelPick{decode_fp8_kernel<64, kTurbo>, Ring<64, kTurbo>::BYTES + 1024};
     if (sh->D == 128) {
         if (nh == 4)
             return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<128, 0, 4>, UmLayout<128, 0>::BYTES}
@@ -1516,11 +1540,11 @@ KernelPick pick_kernel(const FkvDecodeShape* sh, bool turbo, int nh) {
         if (nh == 8)
             return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<128, 0, 8>, UmLayout<128, 0>::BYTES}
                                     : KernelPick{decode_fp8_kernel<128, 32, 8>, UmLayout<128, 32>::BYTES};
-        return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<128, 0>, Ring<128, 0>::BYTES}
-                                : KernelPick{decode_fp8_kernel<128, 32>, Ring<128, 32>::BYTES};
+        return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<128, 0>, Ring<128, 0>::BYTES + 1024}
+                                : KernelPick{decode_fp8_kernel<128, 32>, Ring<128, 32>::BYTES + 1024};
     }
-    return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<64, 0>, Ring<64, 0>::BYTES}
-                            : KernelPick{decode_fp8_kernel<64, 32>, Ring<64, 32>::BYTES};
+    return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<64, 0>, Ring<64, 0>::BYTES + 1024}
+                            : KernelPick{decode_fp8_kernel<64, 32>, Ring<64, 32>::BYTES + 1024};
 }
 
 int resident_for(const FkvDecodeShape* sh, bool turbo, int nh = -1) {
@@ -1529,11 +1553,10 @@ int resident_for(const FkvDecodeShape* sh, bool turbo, int nh = -1) {
     return resident_ctas(k.fn, k.smem, nh > 0 ? (int)UmLayout<128, 0>::TMEM_COLS : 0);
 }
 
-// Tensor map of the far K codes as a (B*Hk*F, D) byte matrix read in boxes of
-// 128 rows with the 128-byte swizzle (the UMMA A-operand layout).  The driver
-// entry point is resolved once; false = unavailable (caller takes the
-// mma.sync path).
-bool far_k_tensor_map(const uint8_t* far_k, int64_t rows, int D, CUtensorMap* out) {
+// Tensor-map encoding (cuTensorMapEncodeTiled, resolved once through the
+// runtime's driver entry point) with a small per-thread cache: a decode loop
+// re-uses the same tier buffers call after call.
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;
     std::call_once(once, [] {
@@ -1543,14 +1566,54 @@ bool far_k_tensor_map(const uint8_t* far_k, int64_t rows, int D, CUtensorMap* ou
             q == cudaDriverEntryPointSuccess)
             fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
     });
-    if (fn == nullptr) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)D};
-    const cuuint32_t box[2] = {(cuuint32_t)D, 128u};
+    return fn;
+}
+
+// 2-D map of a (rows, inner) row-major matrix with row pitch `pitch` bytes,
+// read in (box_inner x box_rows) boxes with the 128-byte swizzle
+bool encode_map(CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t rows,
+                uint64_t pitch, uint32_t box_inner, uint32_t box_rows, CUtensorMap* out) {
+    struct Entry {
+        const void* base;
+        uint64_t inner, rows, pitch;
+        uint32_t bi, br;
+        int dt;
+        CUtensorMap map;
+    };
+    static thread_local std::vector<Entry> cache;
+    for (const Entry& e : cache)
+        if (e.base == base && e.inner == inner && e.rows == rows && e.pitch == pitch && e.bi == box_inner &&
+            e.br == box_rows && e.dt == (int)dt) {
+            *out = e.map;
+            return true;
+        }
+    PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+    if (fn == nullptr || base == nullptr || rows == 0) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)pitch};
+    const cuuint32_t box[2] = {box_inner, box_rows};
     const cuuint32_t es[2] = {1u, 1u};
-    return fn(out, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(far_k), dims, strides, box, es,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    if (fn(out, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    if (cache.size() >= 64) cache.erase(cache.begin());
+    cache.push_back(Entry{base, inner, rows, pitch, box_inner, box_rows, (int)dt, *out});
+    return true;
+}
+
+// far K codes as a (B*Hk*F, D) byte matrix in boxes of 128 rows (the UMMA
+// A-operand layout); false = unavailable (caller takes the mma.sync path)
+bool far_k_tensor_map(const uint8_t* far_k, int64_t rows, int D, CUtensorMap* out) {
+    return encode_map(CU_TENSOR_MAP_DATA_TYPE_UINT8, far_k, (uint64_t)D, (uint64_t)rows, (uint64_t)D,
+                      (uint32_t)D, 128u, out);
+}
+
+// fp16 (rows, D) matrix (near tier, decode buffer) in boxes of 64 rows x 64
+// halves (128 bytes)
+bool fp16_tensor_map(const uint16_t* base, int64_t rows, int D, CUtensorMap* out) {
+    return encode_map(CU_TENSOR_MAP_DATA_TYPE_UINT16, base, (uint64_t)D, (uint64_t)rows,
+                      (uint64_t)D * 2, 64u, 64u, out);
 }
 
 struct Plan {
@@ -1629,7 +1692,7 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 // Opt every kernel instantiation into its dynamic shared memory once per
 // device, then launch.
 int launch_kernel(KernelFn kern, int smem, dim3 grid, const DecodeParams& p, cudaStream_t st,
-                  const CUtensorMap& kmap) {
+                  const TMaps& maps) {
     static thread_local std::vector<std::pair<int, const void*>> done;
     int dev = 0;
     FKV_CUDA_CHECK(cudaGetDevice(&dev));
@@ -1638,7 +1701,7 @@ int launch_kernel(KernelFn kern, int smem, dim3 grid, const DecodeParams& p, cud
         FKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         done.push_back(key);
     }
-    kern<<<grid, kThreads, smem, st>>>(p, kmap);
+    kern<<<grid, kThreads, smem, st>>>(p, maps);
     FKV_LAUNCH_CHECK();
     return FKV_OK;
 }
@@ -1646,10 +1709,23 @@ int launch_kernel(KernelFn kern, int smem, dim3 grid, const DecodeParams& p, cud
 int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws_bytes,
            cudaStream_t st, bool turbo = false) {
     int nh = um_heads(sh, turbo);
-    CUtensorMap kmap;
-    std::memset(&kmap, 0, sizeof(kmap));
-    if (nh > 0 && !far_k_tensor_map(p.far_k, (int64_t)sh->B * sh->Hk * sh->n_far, sh->D, &kmap))
+    TMaps maps;
+    std::memset(&maps, 0, sizeof(maps));
+    if (nh > 0 && !far_k_tensor_map(p.far_k, (int64_t)sh->B * sh->Hk * sh->n_far, sh->D, &maps.far_k))
         nh = 0;
+    {
+        const int64_t bh = (int64_t)sh->B * sh->Hk;
+        FKV_REQUIRE(bh * std::max(sh->n_near_alloc, sh->dec_stride) < ((int64_t)1 << 31), FKV_ERR_UNSUPPORTED,
+                    "near / decode rows exceed the tensor-map coordinate range");
+        if (sh->n_near_alloc > 0)
+            FKV_REQUIRE(fp16_tensor_map(p.near_k, bh * sh->n_near_alloc, sh->D, &maps.near_k) &&
+                            fp16_tensor_map(p.near_v, bh * sh->n_near_alloc, sh->D, &maps.near_v),
+                        FKV_ERR_CUDA, "cuTensorMapEncodeTiled failed for the near tier");
+        if (sh->n_dec > 0)
+            FKV_REQUIRE(fp16_tensor_map(p.dec_k, bh * sh->dec_stride, sh->D, &maps.dec_k) &&
+                            fp16_tensor_map(p.dec_v, bh * sh->dec_stride, sh->D, &maps.dec_v),
+                        FKV_ERR_CUDA, "cuTensorMapEncodeTiled failed for the decode buffer");
+    }
     const KernelPick kp = pick_kernel(sh, turbo, nh);
     const Plan pl =
         make_plan(sh, resident_ctas(kp.fn, kp.smem, nh > 0 ? (int)UmLayout<128, 0>::TMEM_COLS : 0), turbo);
@@ -1686,7 +1762,7 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
             turbo_qproj_kernel<64><<<qg, kQpThreads, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj, BH);
         FKV_LAUNCH_CHECK();
     }
-    return launch_kernel(kp.fn, kp.smem, grid, p, st, kmap);
+    return launch_kernel(kp.fn, kp.smem, grid, p, st, maps);
 }
 
 int fill_common(const FkvDecodeShape* sh, DecodeParams& p, const uint16_t* near_k,
