@@ -64,7 +64,7 @@ struct DecodeParams {
     const float* turbo_s;
     float qjl_coef;
     int B, Hq, Hk, G, HG, Np, F, n_dec, dec_stride, splits, chunk;
-    int near_w;           // cost units of an fp16 near / decode token (a far token is 1)
+    int near_w, far_w;    // cost units of an fp16 near / decode token and of a far token
     float margin, qscale;
 };
 
@@ -1023,25 +1023,27 @@ __global__ void __launch_bounds__(kThreads, 3)
         }
         fence_mbar_init();
     }
-    // segments of this split's chunk [t0, t1) of [near valid | far | decode]
-    // splits are even in cost units (an fp16 near / decode token weighs
-    // near_w, a compressed far token 1); map this split's cost range back to
-    // tokens
-    const int64_t nw = p.near_w;
-    auto to_tok = [&](int64_t cu) -> int {
-        if (cu <= nw * p.Np) return (int)(cu / nw);
-        if (cu <= nw * p.Np + p.F) return (int)(cu - nw * p.Np) + p.Np;
-        return p.Np + p.F + (int)((cu - nw * p.Np - p.F) / nw);
-    };
-    const int64_t total_cost = nw * p.Np + p.F + nw * p.n_dec;
-    const int t0 = to_tok(min((int64_t)split * p.chunk, total_cost));
-    const int t1 = to_tok(min((int64_t)(split + 1) * p.chunk, total_cost));
+    // segments of this split's share of the stream's work: the stream's
+    // tokens [near valid | far | decode], weighted near_w / far_w / near_w
+    // cost units, are cut into p.splits equal cost ranges (the near tier
+    // counts only its near_valid rows, read here)
     const int nv = min(max(__ldg(p.near_valid + s), 0), p.Np);
+    const int64_t nw = p.near_w, fw = p.far_w;
+    const int64_t cost_near = nw * nv, cost_nf = cost_near + fw * p.F,
+                  total_cost = cost_nf + nw * p.n_dec;
+    auto to_tok = [&](int64_t cu) -> int {
+        if (cu <= cost_near) return (int)(cu / nw);
+        if (cu <= cost_nf) return nv + (int)((cu - cost_near) / fw);
+        return nv + p.F + (int)((cu - cost_nf) / nw);
+    };
+    const int64_t chunk = (total_cost + p.splits - 1) / p.splits;
+    const int t0 = to_tok(min((int64_t)split * chunk, total_cost));
+    const int t1 = to_tok(min((int64_t)(split + 1) * chunk, total_cost));
     Segs sg;
-    sg.a[0] = t0;                       sg.e[0] = min(t1, nv);
-    sg.a[1] = max(t0, p.Np) - p.Np;     sg.e[1] = min(t1, p.Np + p.F) - p.Np;
-    sg.a[2] = max(t0, p.Np + p.F) - p.Np - p.F;
-    sg.e[2] = min(t1, p.Np + p.F + p.n_dec) - p.Np - p.F;
+    sg.a[0] = t0;                    sg.e[0] = min(t1, nv);
+    sg.a[1] = max(t0, nv) - nv;      sg.e[1] = min(t1, nv + p.F) - nv;
+    sg.a[2] = max(t0, nv + p.F) - nv - p.F;
+    sg.e[2] = min(t1, nv + p.F + p.n_dec) - nv - p.F;
     sg.n[0] = sg.e[0] > sg.a[0] ? (sg.e[0] - sg.a[0] + RG::NEAR_TOK - 1) / RG::NEAR_TOK : 0;
     sg.n[1] = sg.e[1] > sg.a[1] ? (sg.e[1] - sg.a[1] + RG::FAR_TOK - 1) / RG::FAR_TOK : 0;
     sg.n[2] = sg.e[2] > sg.a[2] ? (sg.e[2] - sg.a[2] + RG::NEAR_TOK - 1) / RG::NEAR_TOK : 0;
@@ -1620,20 +1622,22 @@ struct Plan {
     int HG, splits, chunk;
     size_t rec_bytes, ticket_bytes;
     size_t qproj_bytes;   // turbo only: (B*Hq, 2D) f32 after the counters
-    int near_w;
+    int near_w, far_w;
 };
 
-// Cost model (measured on B200): an fp8 far token is the unit and an fp16
-// near / decode token costs 2; a TurboQuant far token costs about as much as
-// an fp16 one, so there both weigh 1 and the fixed costs shrink accordingly.
+// Cost model (measured on B200, per token): an fp16 near / decode token costs
+// ~1.65x an fp8 / INT4 far token (weights 5 : 3) and ~0.8x a TurboQuant far
+// token (4 : 5).  Fixed costs are in units of far tokens times far_w.
 Plan make_plan(const FkvDecodeShape* sh, int resident, bool turbo = false) {
     Plan pl{};
     const int G = sh->Hq / sh->Hk;
     pl.HG = (G + kHeadsPerTile - 1) / kHeadsPerTile;
-    pl.near_w = turbo ? 1 : 2;
-    const double fixed = turbo ? 300.0 : 512.0, per_split = turbo ? 4.0 : 8.0;
-    // work of a (b, kv head) stream in cost units
-    const int64_t T = pl.near_w * ((int64_t)sh->n_near_alloc + sh->n_dec) + sh->n_far;
+    pl.near_w = turbo ? 4 : 5;
+    pl.far_w = turbo ? 5 : 3;
+    const double fixed = (turbo ? 240.0 : 512.0) * pl.far_w, per_split = (turbo ? 3.0 : 8.0) * pl.far_w;
+    // work of a (b, kv head) stream in cost units (the near tier counted at
+    // its allocation; each CTA later splits its stream's actual rows)
+    const int64_t T = pl.near_w * ((int64_t)sh->n_near_alloc + sh->n_dec) + (int64_t)pl.far_w * sh->n_far;
     const int64_t streams = (int64_t)sh->B * sh->Hk * pl.HG;
     int splits = sh->num_splits;
     if (splits <= 0) {
@@ -1648,7 +1652,7 @@ Plan make_plan(const FkvDecodeShape* sh, int resident, bool turbo = false) {
         splits = 1;
         for (int sp = 1; sp <= 64; ++sp) {
             const int64_t chunk_tok = (T + sp - 1) / sp;
-            if (sp > 1 && chunk_tok < 256) break;
+            if (sp > 1 && chunk_tok < 256 * pl.far_w) break;
             const int64_t waves = (streams * sp + slots - 1) / slots;
             const double cost = (double)waves * ((double)chunk_tok + fixed) + per_split * sp;
             if (cost < best * 0.999) {
@@ -1737,7 +1741,7 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     FKV_REQUIRE(aligned16(workspace), FKV_ERR_INVALID, "workspace must be 16-byte aligned");
     p.B = sh->B; p.Hq = sh->Hq; p.Hk = sh->Hk; p.G = sh->Hq / sh->Hk; p.HG = pl.HG;
     p.Np = sh->n_near_alloc; p.F = sh->n_far; p.n_dec = sh->n_dec; p.dec_stride = sh->dec_stride;
-    p.splits = pl.splits; p.chunk = pl.chunk; p.near_w = pl.near_w; p.margin = sh->spike_margin;
+    p.splits = pl.splits; p.chunk = pl.chunk; p.near_w = pl.near_w; p.far_w = pl.far_w; p.margin = sh->spike_margin;
     p.qscale = (float)(1.0 / sqrt((double)sh->D));   // same f32 constant as the host oracle
     // split counters at the front, split records at the back: a workspace
     // shared by calls of different shapes keeps every counter at zero as long
