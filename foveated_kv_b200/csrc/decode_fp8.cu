@@ -88,62 +88,77 @@ struct RecLayout {
     static constexpr int SIZE = 40 + 8 * D;   // floats
 };
 
-// q pieces of the tensor-core far path from a lane's scaled q values: lane
-// (r, c) holds head r of the CTA's group (zero when absent), dims
-// [c*D/4, (c+1)*D/4).  With e = 2^E chosen so that max|q| e lies in
-// [128, 256), piece 0 = e4m3(q e) and piece j+1 = e4m3(16 (r_j - piece_j)) of
-// the residual r_j; then q = sum_j piece_j 16^-j / e up to 2^-16 relative per
-// element, and a score is (acc_0 + acc_1/16 + acc_2/256 + acc_3/4096) / e.
-// Piece j of head r is row j*NH + r of the B operand (K-major rows of D bytes
-// in the 128-byte swizzle).
+// q pieces of the tensor-core far path, built by one of two warps (half of
+// the NH heads each; lane l covers dims [4l, 4l + 4)).  With e = 2^E chosen
+// so that max|q| e over the CTA's heads lies in [128, 256) (both warps compute
+// the same maximum), piece 0 = e4m3(q e) and piece j+1 = e4m3(16 (r_j -
+// piece_j)) of the residual r_j; then q = sum_j piece_j 16^-j / e up to 2^-16
+// relative per element, and a score is (acc_0 + acc_1/16 + acc_2/256 +
+// acc_3/4096) / e.  Piece j of head hh is row j*NH + hh of the B operand
+// (K-major rows of D bytes in the 128-byte swizzle); *escale = 1/e.
 constexpr int kQPieces = 4;
 
 template <int D, int NH>
-__device__ __forceinline__ void build_q_pieces_from(const float (&qv)[D / 4], int lane,
-                                                    uint8_t* __restrict__ qb, float* escale) {
+__device__ __forceinline__ void build_q_pieces(const DecodeParams& p, int s, int hg, int half,
+                                               int lane, uint8_t* __restrict__ qb, float* escale) {
     static_assert(D == 128, "tensor-core far path assumes 128-byte K rows");
-    constexpr int KC = D / 4;
-    const int r = lane >> 2, c = lane & 3;
+    const int b = s / p.Hk, h = s % p.Hk;
+    const int d0 = 4 * lane;
+    float q4[NH][4];
+#pragma unroll
+    for (int hh = 0; hh < NH; ++hh) {
+        const int g = hg * kHeadsPerTile + hh;
+        q4[hh][0] = q4[hh][1] = q4[hh][2] = q4[hh][3] = 0.f;
+        if (g < p.G) {
+            const uint2 w = __ldg(reinterpret_cast<const uint2*>(
+                p.q + ((int64_t)b * p.Hq + (int64_t)h * p.G + g) * D + d0));
+            const float2 f01 = __half22float2(u32_as_h2(w.x)), f23 = __half22float2(u32_as_h2(w.y));
+            q4[hh][0] = f01.x * p.qscale; q4[hh][1] = f01.y * p.qscale;
+            q4[hh][2] = f23.x * p.qscale; q4[hh][3] = f23.y * p.qscale;
+        }
+    }
     float mx = 0.f;
 #pragma unroll
-    for (int u = 0; u < KC; ++u) mx = fmaxf(mx, fabsf(qv[u]));
+    for (int hh = 0; hh < NH; ++hh)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) mx = fmaxf(mx, fabsf(q4[hh][e]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     int ex = 0;
-    frexpf(mx, &ex);                                  // mx < 2^ex
+    frexpf(mx, &ex);                                      // mx < 2^ex
     const float sc = mx > 0.f ? ldexpf(1.f, 8 - ex) : 1.f;
-    if (lane == 0) *escale = 1.f / sc;                // exact: a power of two
-    if (r >= NH) return;
+    if (half == 0 && lane == 0) *escale = 1.f / sc;       // exact: a power of two
 #pragma unroll
-    for (int v = 0; v < KC / 4; ++v) {
-        const int d0 = c * KC + 4 * v;
+    for (int j2 = 0; j2 < NH / 2; ++j2) {
+        const int hh = half * (NH / 2) + j2;
         float rv[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) rv[e] = qv[4 * v + e] * sc;
+        for (int e = 0; e < 4; ++e) rv[e] = (half ? q4[NH / 2 + j2][e] : q4[j2][e]) * sc;
 #pragma unroll
         for (int j = 0; j < kQPieces; ++j) {
-            uint32_t word = 0;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const __nv_fp8_storage_t code = __nv_cvt_float_to_fp8(rv[e], __NV_SATFINITE, __NV_E4M3);
-                word |= (uint32_t)code << (8 * e);
-                const float back = __half2float(__half(__nv_cvt_fp8_to_halfraw(code, __NV_E4M3)));
-                rv[e] = (rv[e] - back) * 16.f;      // exact residual, scaled up
-            }
-            const int n = j * NH + r;               // B row
-            *reinterpret_cast<uint32_t*>(qb + n * 128 + ((((d0 >> 4) ^ (n & 7)) << 4) | (d0 & 15))) = word;
+            // hardware conversions: f32 pairs -> E4M3x2 (round to nearest
+            // even, saturating) and back E4M3x2 -> f16x2 (exact)
+            uint16_t p01, p23;
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;\n" : "=h"(p01) : "f"(rv[0]), "f"(rv[1]));
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %2, %1;\n" : "=h"(p23) : "f"(rv[2]), "f"(rv[3]));
+            const float2 b01 = __half22float2(u32_as_h2(e4m3x2_to_h2(p01)));
+            const float2 b23 = __half22float2(u32_as_h2(e4m3x2_to_h2(p23)));
+            rv[0] = (rv[0] - b01.x) * 16.f;               // exact residuals, scaled up
+            rv[1] = (rv[1] - b01.y) * 16.f;
+            rv[2] = (rv[2] - b23.x) * 16.f;
+            rv[3] = (rv[3] - b23.y) * 16.f;
+            const int n = j * NH + hh;                    // B row
+            *reinterpret_cast<uint32_t*>(qb + n * 128 + ((((d0 >> 4) ^ (n & 7)) << 4) | (d0 & 15))) =
+                (uint32_t)p01 | ((uint32_t)p23 << 16);
         }
     }
 }
 
 // q A-fragments of the CTA's head group, one uint4 per (k-step, lane), built
 // once by consumer warp 0 into shared memory and read by every consumer warp
-// With NH > 0 the same registers also give the tensor-core far path's q
-// pieces (build_q_pieces_from).
-template <int D, int NH = 0>
+template <int D>
 __device__ __forceinline__ void build_q_frags(const DecodeParams& p, int s, int hg, int lane,
-                                              uint4* __restrict__ qs, uint8_t* __restrict__ qb = nullptr,
-                                              float* escale = nullptr) {
+                                              uint4* __restrict__ qs) {
     const int r = lane >> 2, c = lane & 3;
     const int b = s / p.Hk, h = s % p.Hk;
     const int g = hg * kHeadsPerTile + r;
@@ -165,7 +180,6 @@ __device__ __forceinline__ void build_q_frags(const DecodeParams& p, int s, int 
 #pragma unroll
         for (int u = 0; u < KC; ++u) qv[u] = 0.f;
     }
-    if constexpr (NH > 0) build_q_pieces_from<D, NH>(qv, lane, qb, escale);
 #pragma unroll
     for (int j = 0; j < D / 16; ++j) {
         __half hi[4], lo[4];
@@ -224,7 +238,7 @@ struct UmLayout {
     static constexpr int QREADY = MMAB + kStages * 8;
     static constexpr int DRAIN = QREADY + 8;
     static constexpr int TADDR = DRAIN + 8;
-    static constexpr int ESC = TADDR + 4;
+    static constexpr int ESC = TADDR + 4;                        // piece scale
     static constexpr int BYTES = ESC + 4 + 1024;
     static constexpr uint32_t TMEM_COLS = 64;   // kStages x 32 score columns
     static_assert(RG::SLOT % 1024 == 0, "ring slots must keep 1024-byte alignment");
@@ -1018,7 +1032,7 @@ __global__ void __launch_bounds__(kThreads, 3)
         mbar_init(reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR) + 1, 1);
         if constexpr (UM) {
             for (int i = 0; i < kStages; ++i) mbar_init(reinterpret_cast<uint64_t*>(smem + UL::MMAB) + i, 1);
-            mbar_init(reinterpret_cast<uint64_t*>(smem + UL::QREADY), 1);
+            mbar_init(reinterpret_cast<uint64_t*>(smem + UL::QREADY), 3);   // TMEM + 2 piece warps
             mbar_init(reinterpret_cast<uint64_t*>(smem + UL::DRAIN), 1);
         }
         fence_mbar_init();
@@ -1198,11 +1212,18 @@ __global__ void __launch_bounds__(kThreads, 3)
     uint4* qr = qs + RG::QFRAG / 16;
     uint4* qk = qr + RG::QFRAG / 16;
     float* tsum = reinterpret_cast<float*>(smem + RG::TSUM);
+    // start-up work in parallel: warp 0 the mma.sync q fragments (+ turbo
+    // fragments); on the tensor-core path warp 1 allocates TMEM (and frees it
+    // at the end) while warps 2 and 3 build the q-piece B operand
     if (w == 0) {
-        if constexpr (UM) tmem_alloc(reinterpret_cast<uint32_t*>(smem + UL::TADDR), UL::TMEM_COLS);
-        build_q_frags<D, NH>(p, s, hg, lane, qs, smem + UL::QB, reinterpret_cast<float*>(smem + UL::ESC));
+        build_q_frags<D>(p, s, hg, lane, qs);
         if constexpr (VG == kTurbo) build_turbo_frags<D>(p, s, hg, lane, qr, qk, tsum);
-        if constexpr (UM) {
+    }
+    if constexpr (UM) {
+        if (w >= 1) {
+            if (w == 1) tmem_alloc(reinterpret_cast<uint32_t*>(smem + UL::TADDR), UL::TMEM_COLS);
+            else build_q_pieces<D, NH>(p, s, hg, w - 2, lane, smem + UL::QB,
+                                       reinterpret_cast<float*>(smem + UL::ESC));
             fence_proxy_async();   // B operand -> tensor-core reads
             tc_fence_before();
             __syncwarp();
@@ -1356,9 +1377,10 @@ __global__ void __launch_bounds__(kThreads, 3)
     }
     named_sync(1, kConsumerThreads);
     if constexpr (UM) {
-        if (w == 0) {
+        if (w == 1) {
             // all consumer TMEM reads are done (barrier above); wait for the
             // producer's drain commit so no MMA is in flight, then free TMEM
+            // (the allocating warp frees it)
             uint64_t* drain = reinterpret_cast<uint64_t*>(smem + UL::DRAIN);
             for (int i = 0; i < 4; ++i)
                 if (mbar_wait(drain, 0)) break;
