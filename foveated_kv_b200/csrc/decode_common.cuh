@@ -137,14 +137,17 @@ struct WarpState {
     }
 
     // online-softmax update with this lane's N scores of head r (masked =
-    // -inf); returns the unnormalised probabilities in p[].
+    // -inf) whose maximum is lm; returns the unnormalised probabilities in
+    // p[].  The running max m is raised (and l, z, o rescaled) only when the
+    // tile's max exceeds it by more than kLazyNats: numerator and
+    // denominator always share m, so the result is unchanged, and
+    // p = exp(s - m) stays below e^kLazyNats (fp16-safe as P and p*scale).
+    static constexpr float kLazyNats = 8.f;
     template <int N>
-    __device__ __forceinline__ void softmax_step(const float (&s)[N], float (&p)[N], int lane) {
-        float lm = s[0];
-#pragma unroll
-        for (int j = 1; j < N; ++j) lm = fmaxf(lm, s[j]);
+    __device__ __forceinline__ void softmax_step(const float (&s)[N], float (&p)[N], float lm,
+                                                 int lane) {
         const float tmax = quad_max(lm);
-        const bool up = tmax > m;
+        const bool up = tmax > m + kLazyNats;
         if (__any_sync(0xffffffffu, up)) {
             const float mnew = up ? tmax : m;
             const float alpha = (m == -INFINITY) ? 0.f : exp2f((m - mnew) * kLog2e);
@@ -168,6 +171,13 @@ struct WarpState {
             p[j] = exp2f(fmaf(s[j], kLog2e, -mb));   // s = -inf -> 0
             l += p[j];
         }
+    }
+    template <int N>
+    __device__ __forceinline__ void softmax_step(const float (&s)[N], float (&p)[N], int lane) {
+        float lm = s[0];
+#pragma unroll
+        for (int j = 1; j < N; ++j) lm = fmaxf(lm, s[j]);
+        softmax_step(s, p, lm, lane);
     }
 };
 

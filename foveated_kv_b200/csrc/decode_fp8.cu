@@ -408,20 +408,28 @@ __device__ __forceinline__ void far_tail(const float (&sv)[4 * NT],
                                          const uint32_t (&sz)[NT][4], WarpState<D>& st) {
     const int c = lane & 3;
     float s[4 * NT], pr[4 * NT];
+    float lm = -INFINITY;
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int u = u0[t] + (j >> 1) * 8 + 2 * c + (j & 1);
-            const float v = sv[4 * t + j];
-            s[4 * t + j] = u < cnt ? v : -INFINITY;
-            if (u < cnt && v > st.mf) {   // lane's tokens arrive in increasing order
-                st.mf = v;
-                st.af = gbase + u;
-            }
+            s[4 * t + j] = u < cnt ? sv[4 * t + j] : -INFINITY;
+            lm = fmaxf(lm, s[4 * t + j]);
         }
     }
-    st.softmax_step(s, pr, lane);
+    // spike tracker: the lane's values are in token order, so the earliest
+    // index of a new strict maximum is the first j holding it (rare branch)
+    if (lm > st.mf) {
+        int jj = 0;
+#pragma unroll
+        for (int j = 4 * NT - 1; j >= 0; --j)
+            if (s[j] == lm) jj = j;
+        st.mf = lm;
+        const int ut = (NT > 1 && jj >= 4) ? u0[NT - 1] : u0[0];
+        st.af = gbase + ut + ((jj & 3) >> 1) * 8 + 2 * c + (jj & 1);
+    }
+    st.softmax_step(s, pr, lm, lane);
 #pragma unroll
     for (int t = 0; t < NT; ++t) {
         uint32_t pb0, pb1;
@@ -1006,7 +1014,7 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, const float*
 // far-tier q.K on tcgen05 (NH q heads per CTA, D = 128, E4M3 K; maps.far_k
 // is used only then).
 template <int D, int VG, int NH = 0>
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __maxnreg__(NH > 0 ? 128 : 136)
     decode_fp8_kernel(const DecodeParams p, const __grid_constant__ TMaps maps) {
     using R = RecLayout<D>;
     using RG = Ring<D, VG>;
@@ -1522,9 +1530,12 @@ int resident_ctas(KernelFn kern, int smem, int tmem_cols = 0) {
         if (cudaFuncGetAttributes(&fa, (const void*)kern) == cudaSuccess &&
             cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) == cudaSuccess &&
             cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) == cudaSuccess) {
+            // registers are allocated per warp in units of 8 per thread, from
+            // the 16K-register file of the sub-partition the warp runs on
             const int warps = (kThreads + 31) / 32;
-            const int regs_warp = ((fa.numRegs * 32 + 255) / 256) * 256;
-            const int by_regs = 65536 / std::max(1, regs_warp * warps);
+            const int regs_warp = ((fa.numRegs + 7) / 8) * 8 * 32;
+            int by_regs = 0;
+            while (((by_regs + 1) * warps + 3) / 4 * regs_warp <= 16384) ++by_regs;
             const int by_smem = sm_smem / std::max(1, smem + (int)fa.sharedSizeBytes + reserved);
             const int by_threads = 2048 / kThreads;
             const int by_tmem = 512 / tmem_cols;
@@ -1535,18 +1546,7 @@ int resident_ctas(KernelFn kern, int smem, int tmem_cols = 0) {
     return n;
 }
 
-// q heads per CTA on the tensor-core far path (0 = mma.sync path): fp8 K with
-// D = 128, a far tier, row indices inside the tensor map's int32 range, a GQA
-// group of at least two q heads.
-// FKV_QK_PATH=mma in the environment selects the mma.sync path.
-int um_heads(const FkvDecodeShape* sh, bool turbo) {
-    if (turbo || sh->D != 128 || sh->n_far <= 0) return 0;
-    if ((int64_t)sh->B * sh->Hk * sh->n_far >= ((int64_t)1 << 31) - 256) return 0;
-    if (sh->Hq / sh->Hk < 2) return 0;   // one q head: the mma.sync path is a little faster
-    const char* e = std::getenv("FKV_QK_PATH");
-    if (e != nullptr && std::strcmp(e, "mma") == 0) return 0;
-    return (sh->Hq / sh->Hk) <= 4 ? 4 : 8;
-}
+int um_heads(const FkvDecodeShape* sh, bool turbo);
 
 struct KernelPick {
     KernelFn fn;
@@ -1694,6 +1694,27 @@ Plan make_plan(const FkvDecodeShape* sh, int resident, bool turbo = false) {
     pl.ticket_bytes = 16 + (size_t)streams * sizeof(int32_t);   // status word + counters
     pl.qproj_bytes = (size_t)sh->B * sh->Hq * 2 * D * sizeof(float);
     return pl;
+}
+
+// q heads per CTA on the tensor-core far path (0 = mma.sync path).  Eligible:
+// fp8 K with D = 128, a far tier, far rows inside the tensor map's int32
+// range.  Chosen by default when a CTA's planned work is at least
+// kUmMinChunk cost units: on B200 the tensor-core path's CTAs start (TMEM
+// allocation, q pieces, first MMA) and drain about 3 us later while each far
+// token costs a few percent less (c3, ~19K units per CTA: 633 vs 611 us; c4,
+// ~61K per CTA: 312 vs 322 us).  FKV_QK_PATH=mma / tcgen05 forces either.
+constexpr int64_t kUmMinChunk = 40000;
+
+int um_heads(const FkvDecodeShape* sh, bool turbo) {
+    if (turbo || sh->D != 128 || sh->n_far <= 0) return 0;
+    if ((int64_t)sh->B * sh->Hk * sh->n_far >= ((int64_t)1 << 31) - 256) return 0;
+    const int nh = (sh->Hq / sh->Hk) <= 4 ? 4 : 8;
+    const char* e = std::getenv("FKV_QK_PATH");
+    if (e != nullptr && std::strcmp(e, "mma") == 0) return 0;
+    if (e != nullptr && std::strcmp(e, "tcgen05") == 0) return nh;
+    const KernelPick k = pick_kernel(sh, false, nh);
+    const Plan pl = make_plan(sh, resident_ctas(k.fn, k.smem, (int)UmLayout<128, 0>::TMEM_COLS));
+    return pl.chunk >= kUmMinChunk ? nh : 0;
 }
 
 int validate(const FkvDecodeShape* sh) {

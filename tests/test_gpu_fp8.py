@@ -84,25 +84,23 @@ DECODE_CASES = [
 ]
 
 
-@pytest.fixture(params=["auto", "mma"])
+@pytest.fixture(params=["tcgen05", "mma"])
 def qk_path(request, monkeypatch):
-    """Run a decode test on the default q.K path (tcgen05 where the shape
-    allows it) and on the mma.sync path (FKV_QK_PATH=mma)."""
-    if request.param == "mma":
-        monkeypatch.setenv("FKV_QK_PATH", "mma")
-    else:
-        monkeypatch.delenv("FKV_QK_PATH", raising=False)
+    """Run a decode test on each far-tier q.K path: tcgen05 (tensor memory,
+    forced with FKV_QK_PATH=tcgen05 where the shape allows it) and mma.sync
+    (FKV_QK_PATH=mma).  The default picks one per shape by CTA work size."""
+    monkeypatch.setenv("FKV_QK_PATH", request.param)
     return request.param
 
 
 def _expect_path(lay, Hq, path):
     """The library reports the q.K path the launch takes: tcgen05 (4 or 8 q
-    heads per CTA) for D = 128, G >= 2 and a far tier unless forced off."""
+    heads per CTA) for D = 128 with a far tier when forced, else mma.sync."""
     lib = _native.load()
     sh = lay._fill_shape(Hq, lay.spike_margin)
     got = lib.fkv_decode_qk_path(C.byref(sh), lay.far_k.data_ptr())
     G = Hq // lay.near_k.shape[1]
-    want_tc = path == "auto" and lay.near_k.shape[-1] == 128 and G >= 2 and lay.n_far > 0
+    want_tc = path == "tcgen05" and lay.near_k.shape[-1] == 128 and lay.n_far > 0
     assert (got > 0) == want_tc, (got, path, G)
     if want_tc:
         assert got == (4 if G <= 4 else 8)

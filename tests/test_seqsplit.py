@@ -97,8 +97,10 @@ def test_gloo_two_rank_exchange_matches_unsplit():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("path", ["tcgen05", "mma"])
 @pytest.mark.parametrize("P", [1, 2, 3, 8])
-def test_partials_on_one_gpu_equal_unsplit(P):
+def test_partials_on_one_gpu_equal_unsplit(P, path, monkeypatch):
+    monkeypatch.setenv("FKV_QK_PATH", path)   # both far-tier q.K paths in partial mode
     from foveated_kv_b200 import TierConfig, compress_layer
     from foveated_kv_b200.seqsplit import shard_bounds, compress_shard, decode_partial, combine
     S, B, Hk, Hq, D = 4000, 2, 2, 8, 128
