@@ -104,14 +104,18 @@ def compress_shard(k_shard: torch.Tensor, v_shard: torch.Tensor, S: int, lo: int
 
 
 def decode_partial(layer: FoveatedLayer, q: torch.Tensor, far_offset: int):
-    """This shard's partial records: part (B*Hq, D+4) f32, arg (B*Hq) int32."""
+    """This shard's partial records: part (B*Hq, D+4) f32, arg (B*Hq) int32.
+    Both are views of one flat f32 buffer (arg bit-cast), so a single
+    collective can exchange them."""
     lib = _native.load()
     B, Hq, D = q.shape[0], q.shape[1], q.shape[-1]
     qq = q.reshape(B, Hq, D).to(F16).contiguous()
     sh = layer._fill_shape(Hq, layer.spike_margin)
     ws = _Workspace.get(lib.fkv_decode_workspace_bytes(C.byref(sh)), layer.device)
-    part = torch.empty((B * Hq, D + 4), dtype=torch.float32, device=layer.device)
-    arg = torch.empty((B * Hq,), dtype=I32, device=layer.device)
+    N = B * Hq
+    flat = torch.empty((N * (D + 4) + N,), dtype=torch.float32, device=layer.device)
+    part = flat[:N * (D + 4)].view(N, D + 4)
+    arg = flat[N * (D + 4):].view(torch.int32)
     dk = layer._dec_k if layer.n_decode else None
     dv = layer._dec_v if layer.n_decode else None
     _native.check(lib.fkv_decode_fp8_partial(
@@ -122,23 +126,49 @@ def decode_partial(layer: FoveatedLayer, q: torch.Tensor, far_offset: int):
     return part, arg
 
 
+def _joined_view(part: torch.Tensor, arg: torch.Tensor):
+    """The flat [records | argmax] buffer when part and arg are the two views
+    decode_partial makes of it, else None."""
+    N, D4 = part.shape
+    if arg.dtype != torch.int32 or arg.numel() != N or not part.is_contiguous():
+        return None
+    if part.data_ptr() + N * D4 * 4 != arg.data_ptr():
+        return None
+    if part.untyped_storage().data_ptr() != arg.untyped_storage().data_ptr():
+        return None
+    if part.untyped_storage().nbytes() < part.storage_offset() * 4 + (N * D4 + N) * 4:
+        return None
+    return torch.empty((0,), dtype=torch.float32, device=part.device).set_(
+        part.untyped_storage(), part.storage_offset(), (N * D4 + N,), (1,))
+
+
 def gather_partials(part: torch.Tensor, arg: torch.Tensor, group=None):
     """All-gather every rank's records: (P, N, D+4) and (P, N), rank order.
-    NCCL over NVLink on GPUs; any backend works (gloo for host tests)."""
+    One collective when part and arg share one buffer (as decode_partial
+    returns them), two otherwise; NCCL over NVLink on GPUs, any backend works
+    (gloo for host tests)."""
     if not (dist.is_available() and dist.is_initialized()):
         return part[None], arg[None]          # single process: nothing to exchange
     P = dist.get_world_size(group)
-    parts = torch.empty((P * part.shape[0],) + tuple(part.shape[1:]), dtype=part.dtype,
-                        device=part.device)
+    N, D4 = part.shape
+    flat = _joined_view(part, arg)
+    if flat is not None:
+        out = torch.empty((P * (N * D4 + N),), dtype=torch.float32, device=part.device)
+        dist.all_gather_into_tensor(out, flat, group=group)
+        out = out.view(P, N * D4 + N)
+        return (out[:, :N * D4].contiguous().view(P, N, D4),
+                out[:, N * D4:].contiguous().view(torch.int32))
+    parts = torch.empty((P * N, D4), dtype=part.dtype, device=part.device)
     args = torch.empty((P * arg.shape[0],), dtype=arg.dtype, device=arg.device)
     dist.all_gather_into_tensor(parts, part.contiguous(), group=group)
     dist.all_gather_into_tensor(args, arg.contiguous(), group=group)
-    return parts.view((P,) + tuple(part.shape)), args.view(P, -1)
+    return parts.view(P, N, D4), args.view(P, -1)
 
 
 def combine(parts: torch.Tensor, args: torch.Tensor, margin: float):
     """Merge (P, N, D+4) records on the device: out (N, D) fp16, flags, tokens."""
     lib = _native.load()
+    parts, args = parts.contiguous(), args.contiguous()   # the C ABI reads dense arrays
     P, N, D4 = parts.shape
     D = D4 - 4
     out = torch.empty((N, D), dtype=F16, device=parts.device)
