@@ -1663,20 +1663,29 @@ Plan make_plan(const FkvDecodeShape* sh, int resident, bool turbo = false) {
     const int64_t streams = (int64_t)sh->B * sh->Hk * pl.HG;
     int splits = sh->num_splits;
     if (splits <= 0) {
-        // Pick the split count minimising (waves of resident CTAs) x (chunk
-        // length + a fixed per-CTA cost: launch, q fragments, pipeline fill,
-        // record write) + a small cost per split record the last CTA of a
-        // stream merges (bulk copies).  Balances wave quantisation against CTA overhead:
-        // few long CTAs for a handful of (b, kv head) streams, a few splits
-        // for large batches.
-        const int64_t slots = (int64_t)num_sms() * std::max(resident, 1);
+        // Pick the split count minimising the busiest SM's time.  The block
+        // scheduler spreads the CTAs evenly over the SMs; each SM runs its
+        // share in rounds of `resident` CTAs, a round of k co-resident CTAs
+        // progressing at thr(k) CTA-speeds (measured on B200: thr(2) ~ 1.7;
+        // thr(3) ~ 2.3 when the job is throughput-bound, but no better than 2
+        // for small jobs, where the CTAs' start-up and merge latencies
+        // dominate: c1 at S=4K..16K is fastest at 2 CTAs per SM).  Each CTA
+        // also pays a fixed cost (launch, q fragments, pipeline fill, record
+        // write), each split a small merge cost.
+        const int nsm = num_sms();
+        const int res = std::max(resident, 1);
+        const bool small_job = (double)streams * (double)T / nsm < 60000.0;
+        auto thr = [&](int k) { return k <= 1 ? 1.0 : (k == 2 || small_job) ? 1.7 : 2.3; };
         double best = 1e300;
         splits = 1;
         for (int sp = 1; sp <= 64; ++sp) {
             const int64_t chunk_tok = (T + sp - 1) / sp;
             if (sp > 1 && chunk_tok < 256 * pl.far_w) break;
-            const int64_t waves = (streams * sp + slots - 1) / slots;
-            const double cost = (double)waves * ((double)chunk_tok + fixed) + per_split * sp;
+            const int64_t per_sm = (streams * sp + nsm - 1) / nsm;
+            const int64_t full = per_sm / res, rem = per_sm % res;
+            const double cta = (double)chunk_tok + fixed;
+            const double cost = (double)full * res * cta / thr(res) +
+                                (rem ? (double)rem * cta / thr((int)rem) : 0.0) + per_split * sp;
             if (cost < best * 0.999) {
                 best = cost;
                 splits = sp;
