@@ -190,3 +190,34 @@ def test_decode_buffer_growth_and_flags_all_set():
                                            -1e4)
     assert_output_close(np_(out).astype(np.float64)[:, :, 0], rout, "dec40")
     assert np.array_equal(np_(tk), rtk)
+
+
+@pytest.mark.parametrize("splits", [1, 0])
+def test_decode_long_stream_accumulation(splits, qk_path):
+    """One 32K-token stream decoded by as few CTAs as possible (splits=1): the
+    longest per-warp accumulation of P.V, which stresses the f32 accumulator
+    (raw INT4 codes enter the product with their magic-number offsets, removed
+    once per warp record)."""
+    S, B, Hk, Hq, D = 32768, 1, 1, 4, 128
+    w = numpy_workload(31, B, Hk, Hq, S, D, 0)
+    t = _tensors(w)
+    lay = compress_layer(t["k"], t["v"], TierConfig(spike_margin=0.5))
+    lib = _native.load()
+    sh = lay._fill_shape(Hq, 0.5)
+    sh.num_splits = splits
+    ws = torch.zeros(lib.fkv_decode_workspace_bytes(C.byref(sh)) + 16, dtype=torch.uint8,
+                     device=dev)
+    out = torch.empty((B, Hq, D), dtype=torch.float16, device=dev)
+    fl = torch.empty((B, Hq), dtype=torch.int32, device=dev)
+    tk = torch.empty_like(fl)
+    p = lambda x: x.data_ptr()
+    rc = lib.fkv_decode_fp8(C.byref(sh), p(lay.near_k), p(lay.near_v), p(lay.near_valid),
+                            p(lay.far_k), p(lay.far_v), p(lay.far_v_scale), p(lay.far_v_zero),
+                            p(t["q"]), 0, 0, p(out), p(fl), p(tk), p(ws), ws.numel(),
+                            torch.cuda.current_stream().cuda_stream)
+    _native.check(rc, "fkv_decode_fp8")
+    torch.cuda.synchronize()
+    rout, rfl, rtk, diag = O.decode_attend(layer_to_oracle(lay), w["q"], None, None, 0.5)
+    err, cos = assert_output_close(np_(out).astype(np.float64), rout, f"long splits={splits}")
+    print(f"long stream splits={splits} path={qk_path}: max-abs {err:.2e} cos {cos:.7f}")
+    assert assert_spikes_match(np_(fl), np_(tk), rfl, rtk, diag, 0.5) == 0
