@@ -180,10 +180,20 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     group_minmax(mn, mx, width);
     float scale = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
     if (scale == 0.0f) scale = 1.0f;
+    // code = rint((x - mn) / scale) with the IEEE fp32 quotient.  The
+    // quotient lies in [0, ~15]; the product with the rounded reciprocal is
+    // within ~2e-6 of it, so rint agrees unless the product sits within 1e-4
+    // of a rounding boundary (k + 0.5) -- only then (or for non-finite
+    // values) is the correctly rounded division evaluated.
+    const float rcp = __frcp_rn(scale);
     uint32_t packed = 0;
 #pragma unroll
     for (int i = 0; i < N; ++i) {
-        float q = rintf(__fdiv_rn(__fsub_rn(x[i], mn), scale));
+        const float d = __fsub_rn(x[i], mn);
+        float qa = __fmul_rn(d, rcp);
+        const float fr = qa - floorf(qa);
+        if (!(fabsf(fr - 0.5f) > 1e-4f)) qa = __fdiv_rn(d, scale);
+        float q = rintf(qa);
         q = fminf(fmaxf(q, 0.0f), 15.0f);
         packed |= ((uint32_t)q) << (4 * i);
     }

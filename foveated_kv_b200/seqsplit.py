@@ -50,15 +50,22 @@ def shard_bounds_balanced(S: int, rank: int, world: int, cfg: TierConfig):
     return cuts[rank], cuts[rank + 1]
 
 
+def _shard_ranges(S: int, lo: int, hi: int, tb: dict):
+    """Global-tier near ranges (sinks, recent middle, window) and the far range,
+    each clipped to the shard [lo, hi), as (a, b) pairs."""
+    ns, w, ms, me, nms = tb["n_sinks"], tb["window"], tb["mid_start"], tb["mid_end"], tb["near_mid_start"]
+    clip = lambda a, b: (max(a, lo), max(min(b, hi), max(a, lo)))
+    return [clip(0, ns), clip(nms, me), clip(S - w, S)], clip(ms, nms)
+
+
 def shard_positions(S: int, lo: int, hi: int, cfg: TierConfig):
     """Global-tier near / far positions inside [lo, hi) and the global far
     index of the shard's first far token."""
     tb = cfg.tier_boundaries(S)
-    ns, w, ms, me, nms = tb["n_sinks"], tb["window"], tb["mid_start"], tb["mid_end"], tb["near_mid_start"]
-    seg = lambda a, b: np.arange(max(a, lo), min(b, hi), dtype=np.int32)
-    near = np.concatenate([seg(0, ns), seg(nms, me), seg(S - w, S)])
-    far = seg(ms, nms)
-    off = int(far[0] - ms) if far.size else 0
+    near_r, (fa, fb) = _shard_ranges(S, lo, hi, tb)
+    near = np.concatenate([np.arange(a, b, dtype=np.int32) for a, b in near_r])
+    far = np.arange(fa, fb, dtype=np.int32)
+    off = int(far[0] - tb["mid_start"]) if far.size else 0
     return near, far, off, tb
 
 
@@ -70,16 +77,20 @@ def compress_shard(k_shard: torch.Tensor, v_shard: torch.Tensor, S: int, lo: int
     k = k_shard.to(F16).contiguous()
     v = v_shard.to(F16).contiguous()
     B, H, Ssh, D = k.shape
-    near, far, off, tb = shard_positions(S, lo, lo + Ssh, cfg)
-    R = near.size
-    Np = R + max(int(R * cfg.promo_headroom_pct), cfg.promo_headroom_min)
-    Fn = far.size
     dev = k.device
+    tb = cfg.tier_boundaries(S)
+    near_r, (fa, fb) = _shard_ranges(S, lo, lo + Ssh, tb)
+    # index lists built on the device (no host arrays, no host->device copies)
+    near = torch.cat([torch.arange(a - lo, b - lo, dtype=I32, device=dev) for a, b in near_r])
+    R = int(near.numel())
+    Np = R + max(int(R * cfg.promo_headroom_pct), cfg.promo_headroom_min)
+    Fn = fb - fa
+    off = fa - tb["mid_start"] if Fn > 0 else 0
     L = _native.TierLayout()
     L.S, L.n_near_padded, L.far_count, L.r_actual = Ssh, Np, Fn, R
     near_idx = torch.full((B, H, Np), -1, dtype=I32, device=dev)
-    near_idx[:, :, :R] = torch.from_numpy(near - lo).to(dev)
-    far_idx_local = torch.from_numpy(far - lo).to(dev).expand(B, H, Fn).contiguous()
+    near_idx[:, :, :R] = near
+    far_idx_local = torch.arange(fa - lo, fb - lo, dtype=I32, device=dev).expand(B, H, Fn).contiguous()
     near_k = torch.empty((B, H, Np, D), dtype=F16, device=dev)
     near_v = torch.empty_like(near_k)
     far_k = torch.empty((B, H, Fn, D), dtype=U8, device=dev)

@@ -221,3 +221,39 @@ def test_decode_long_stream_accumulation(splits, qk_path):
     err, cos = assert_output_close(np_(out).astype(np.float64), rout, f"long splits={splits}")
     print(f"long stream splits={splits} path={qk_path}: max-abs {err:.2e} cos {cos:.7f}")
     assert assert_spikes_match(np_(fl), np_(tk), rfl, rtk, diag, 0.5) == 0
+
+
+def test_compress_int4_rounding_boundaries():
+    """V rows built so that (v - min) / scale lands exactly on, or next to,
+    the half-integer rounding boundaries of the INT4 codes (where the kernel
+    falls back from the reciprocal product to the correctly rounded division):
+    codes must still equal the oracle's bit for bit."""
+    rng = np.random.default_rng(3)
+    B, H, S, D = 1, 2, 400, 128
+    w = numpy_workload(41, B, H, 4, S, D, 0)
+    v = w["v"].copy()
+    for h in range(H):
+        for s in range(S):
+            kind = s % 4
+            k = rng.integers(0, 15, D).astype(np.float64)
+            if kind == 0:      # scale 1: exact ties k + 0.5
+                row = k + 0.5
+                row[0], row[1] = 0.0, 15.0
+            elif kind == 1:    # scale 0.5, min -3: exact ties
+                row = -3.0 + 0.5 * (k + 0.5)
+                row[0], row[1] = -3.0, 4.5
+            elif kind == 2:    # scale 1/15 (inexact): fp16 values next to the ties
+                row = (k + 0.5) / 15.0
+                row[0], row[1] = 0.0, 1.0
+            else:              # ordinary data
+                continue
+            v[0, h, s] = row.astype(np.float16)
+    w["v"] = v
+    cfg = TierConfig(window_size=16)
+    ref = O.compress_layer(w["k"], w["v"], _cfg_dict(cfg))
+    t = _tensors(w)
+    lay = compress_layer(t["k"], t["v"], cfg)
+    torch.cuda.synchronize()
+    for f in ["far_v", "far_v_scale", "far_v_zero", "far_k"]:
+        a, b = bits(np_(getattr(lay, f))), bits(ref[f])
+        assert np.array_equal(a, b), f"{f} differs at {np.argwhere(a != b)[:5]}"
