@@ -20,31 +20,28 @@ namespace {
 
 constexpr int kWarpsPerBlock = 8;
 
-// fp16 bits -> E4M3 code, identical to _fp16_to_e4m3 (mlx_foveated.py:528-566):
-// rebias -8, round-half-even 10->3 bits with carry, underflow after carry (or
-// fp16 exponent 0) -> signed zero, overflow / inf / nan -> sign|0x76.
-__device__ __forceinline__ uint32_t f16_to_e4m3(uint32_t bits) {
-    const uint32_t sign = (bits >> 15) & 1u;
-    const int exp16 = (bits >> 10) & 0x1F;
-    const uint32_t mant16 = bits & 0x3FFu;
-    int exp8 = exp16 - 8;
-    const uint32_t trunc = mant16 >> 7;
-    const uint32_t rb = (mant16 >> 6) & 1u;
-    const uint32_t sticky = (mant16 & 0x3Fu) != 0u;
-    uint32_t mant3 = trunc + (rb & (sticky | (trunc & 1u)));
-    if (mant3 >= 8u) {
-        mant3 = 0u;
-        exp8 += 1;
+// Two fp16 values (low half first) -> two E4M3 codes (low byte first),
+// identical to _fp16_to_e4m3 (mlx_foveated.py:528-566: rebias -8, round-half-
+// even 10->3 bits with carry, underflow after carry -> signed zero, overflow /
+// inf / nan -> sign|0x76).  The hardware conversion (round to nearest even,
+// saturating) agrees with that rounding on the normal range; the reference's
+// own edges are applied on the fp16 magnitude: below 0x23C0
+// (0.96875 * 2^-6, where the reference's rounded exponent is still <= 0) a
+// signed zero, from 0x5BC0 (248, whose rounding carries into exponent 15)
+// and for inf / NaN the code sign|0x76.  All 65,536 patterns are tested.
+__device__ __forceinline__ uint32_t f16x2_to_e4m3x2(uint32_t w) {
+    uint16_t hw;
+    asm("cvt.rn.satfinite.e4m3x2.f16x2 %0, %1;\n" : "=h"(hw) : "r"(w));
+    uint32_t out = 0;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const uint32_t mag = (w >> (16 * j)) & 0x7FFFu;
+        const uint32_t sgn = (w >> (16 * j + 8)) & 0x80u;
+        uint32_t byte = ((uint32_t)hw >> (8 * j)) & 0xFFu;
+        byte = mag < 0x23C0u ? sgn : (mag >= 0x5BC0u ? (sgn | 0x76u) : byte);
+        out |= byte << (8 * j);
     }
-    if (exp8 <= 0 || exp16 == 0) {
-        exp8 = 0;
-        mant3 = 0u;
-    }
-    if (exp8 >= 15 || exp16 == 31) {
-        exp8 = 14;
-        mant3 = 6u;
-    }
-    return (sign << 7) | ((uint32_t)exp8 << 3) | mant3;
+    return out;
 }
 
 __device__ __forceinline__ float h2f(uint16_t b) { return __half2float(__ushort_as_half(b)); }
@@ -163,7 +160,8 @@ __global__ void __launch_bounds__(kWarpsPerBlock * 32)
     // K: E4M3 codes, lane owns dims [lane*N, lane*N+N)
     uint32_t kc = 0;
 #pragma unroll
-    for (int i = 0; i < N; ++i) kc |= f16_to_e4m3(a.h[i]) << (8 * i);
+    for (int i = 0; i < N; i += 2)
+        kc |= f16x2_to_e4m3x2((uint32_t)a.h[i] | ((uint32_t)a.h[i + 1] << 16)) << (8 * i);
     if constexpr (N == 4) reinterpret_cast<uint32_t*>(far_k + frow * D)[lane] = kc;
     else reinterpret_cast<uint16_t*>(far_k + frow * D)[lane] = (uint16_t)kc;
 

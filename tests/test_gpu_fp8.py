@@ -257,3 +257,25 @@ def test_compress_int4_rounding_boundaries():
     for f in ["far_v", "far_v_scale", "far_v_zero", "far_k"]:
         a, b = bits(np_(getattr(lay, f))), bits(ref[f])
         assert np.array_equal(a, b), f"{f} differs at {np.argwhere(a != b)[:5]}"
+
+
+def test_compress_fp8_all_fp16_patterns():
+    """Every one of the 65,536 fp16 bit patterns (zeros, subnormals, the
+    underflow and overflow boundaries, inf, NaN) goes through the device fp8
+    encoder as far-tier K and must give the oracle's E4M3 code (the
+    reference's _fp16_to_e4m3 semantics, pinned by the golden table)."""
+    S, D = 600, 128
+    w = numpy_workload(5, 1, 1, 1, S, D, 0)
+    pats = np.arange(65536, dtype=np.uint32).astype(np.uint16).view(np.float16).reshape(512, D)
+    k = w["k"].copy()
+    k[0, 0, 4:4 + 512] = pats
+    cfg = TierConfig(near_pct=0.0, window_size=8)
+    t = _tensors({"k": k, "v": w["v"]})
+    lay = compress_layer(t["k"], t["v"], cfg)
+    torch.cuda.synchronize()
+    far_idx = np_(lay.far_idx)[0, 0]
+    assert far_idx[0] == 4 and np.all(np.diff(far_idx) == 1)
+    got = np_(lay.far_k)[0, 0, :512].reshape(-1)
+    want = O.fp16_to_e4m3(pats.reshape(-1))
+    bad = np.argwhere(got != want).reshape(-1)
+    assert bad.size == 0, [(hex(int(pats.reshape(-1).view(np.uint16)[i])), hex(int(got[i])), hex(int(want[i]))) for i in bad[:8]]
