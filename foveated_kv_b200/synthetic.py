@@ -55,7 +55,7 @@ def torch_workload(seed: int, B: int, Hk: int, Hq: int, S: int, D: int, n_dec: i
     return {"k": k, "v": v, "q": q, "q_obs": q_obs, "dec_k": dk, "dec_v": dv}
 
 
-# BASELINE configurations (shapes only; see DESIGN.md for the workload table).
+# The benchmark configurations c0-c4 (shapes, tier settings, far-tier kind).
 CONFIGS = {
     "c0": dict(B=1, Hq=14, Hk=2, D=64, S=1024, n_dec=16, near_pct=0.10, n_sinks=4,
                window_size=64, select="importance", v_group=32, compress_method="fp8"),
