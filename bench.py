@@ -114,10 +114,12 @@ def build_layer(cfgname, seed, device, batch=0):
     w = torch_workload(seed, c["B"], c["Hk"], c["Hq"], c["S"], c["D"], c["n_dec"], device)
     cfg = TierConfig(near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
                      v_group=c["v_group"], compress_method=c["compress_method"],
-                     spike_margin=0.5)
+                     select=c["select"], spike_margin=0.5)
     if cfgname == "c3":
         inject_spikes(w, cfg, seed)
-    lay = compress_layer(w["k"], w["v"], cfg)
+    # importance selection (c0) scores tokens with the seeded query
+    lay = compress_layer(w["k"], w["v"], cfg,
+                         query=w["q"] if c["select"] == "importance" else None)
     for i in range(c["n_dec"]):
         lay.add_token(w["dec_k"][:, :, i:i + 1], w["dec_v"][:, :, i:i + 1])
     q = w["q"]
@@ -159,7 +161,8 @@ class CpuArm:
         self.w = numpy_workload(7, self.seqs, c["Hk"], c["Hq"], c["S"], c["D"], c["n_dec"])
         self.lay = O.compress_layer(self.w["k"], self.w["v"], dict(
             near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
-            v_group=c["v_group"], compress_method=c["compress_method"]))
+            v_group=c["v_group"], compress_method=c["compress_method"], select=c["select"]),
+            q_obs=self.w["q"] if c["select"] == "importance" else None)
 
     def run(self):
         t0 = time.perf_counter()
@@ -462,6 +465,7 @@ def main():
             "data": "synthetic (seeded N(0,1) fp16, 4 outlier K channels/head, 1% spikes)",
             "config": {"workload": args.config, "B_per_gpu": B, "Hq": Hq, "Hk": Hk, "D": D,
                        "S": c["S"], "near_pct": c["near_pct"], "window": c["window_size"],
+                       "select": c["select"],
                        "far_tier": ("TurboQuant 2-bit K + 1-bit QJL, 2-bit V/32" if
                                     cfg.compress_method == "turbo" else
                                     "fp8 E4M3 K + INT4 V (" + ("per token" if c["v_group"] is None
