@@ -629,6 +629,9 @@ __global__ void __launch_bounds__(kQpThreads)
                        const float* __restrict__ Sm, float* __restrict__ out, int BH) {
     __shared__ __align__(16) float mrow[kQpRows][D + 4];
     __shared__ __align__(16) float qv[kQpHeads][D + 4];
+    // the decode kernel launched next may start now: only its warp that reads
+    // these projections waits for this grid (griddepcontrol.wait)
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int o0 = blockIdx.x * kQpRows, h0 = blockIdx.y * kQpHeads;
     const int tid = threadIdx.x;
     for (int i = tid; i < kQpRows * D / 4; i += kQpThreads) {
@@ -1225,7 +1228,12 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
     // at the end) while warps 2 and 3 build the q-piece B operand
     if (w == 0) {
         build_q_frags<D>(p, s, hg, lane, qs);
-        if constexpr (VG == kTurbo) build_turbo_frags<D>(p, s, hg, lane, qr, qk, tsum);
+        if constexpr (VG == kTurbo) {
+            // q Pi^T / q S^T come from turbo_qproj_kernel, which may still be
+            // running (programmatic dependent launch): wait for it here only
+            asm volatile("griddepcontrol.wait;\n" ::: "memory");
+            build_turbo_frags<D>(p, s, hg, lane, qr, qk, tsum);
+        }
     }
     if constexpr (UM) {
         if (w >= 1) {
@@ -1748,7 +1756,7 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 // Opt every kernel instantiation into its dynamic shared memory once per
 // device, then launch.
 int launch_kernel(KernelFn kern, int smem, dim3 grid, const DecodeParams& p, cudaStream_t st,
-                  const TMaps& maps) {
+                  const TMaps& maps, bool after_qproj = false) {
     static thread_local std::vector<std::pair<int, const void*>> done;
     int dev = 0;
     FKV_CUDA_CHECK(cudaGetDevice(&dev));
@@ -1757,7 +1765,23 @@ int launch_kernel(KernelFn kern, int smem, dim3 grid, const DecodeParams& p, cud
         FKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         done.push_back(key);
     }
-    kern<<<grid, kThreads, smem, st>>>(p, maps);
+    if (after_qproj) {
+        // programmatic dependent launch: the decode grid may begin (barrier
+        // set-up, first tier copies) while the q-projection kernel finishes
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        FKV_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, p, maps));
+    } else {
+        kern<<<grid, kThreads, smem, st>>>(p, maps);
+    }
     FKV_LAUNCH_CHECK();
     return FKV_OK;
 }
@@ -1818,7 +1842,7 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
             turbo_qproj_kernel<64><<<qg, kQpThreads, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj, BH);
         FKV_LAUNCH_CHECK();
     }
-    return launch_kernel(kp.fn, kp.smem, grid, p, st, maps);
+    return launch_kernel(kp.fn, kp.smem, grid, p, st, maps, turbo);
 }
 
 int fill_common(const FkvDecodeShape* sh, DecodeParams& p, const uint16_t* near_k,
