@@ -162,9 +162,12 @@ int fkv_decode_fp8(const FkvDecodeShape* s, const uint16_t* near_k, const uint16
 /* Which q.K path fkv_decode_fp8 / _partial / _noalloc take for this shape
  * and far_k pointer (no counterpart in the reference, whose Metal kernel has
  * one path): 4 or 8 = q heads per CTA on the 5th-generation tensor cores
- * (tcgen05.mma on the E4M3 codes, scores in tensor memory; D = 128, G >= 2,
- * a far tier), 0 = mma.sync after converting the codes, negative = invalid
- * shape.  The environment variable FKV_QK_PATH=mma forces 0. */
+ * (tcgen05.mma on the E4M3 codes, scores in tensor memory), 0 = mma.sync
+ * after converting the codes, negative = invalid shape.  The tensor-core
+ * path needs D = 128 and a far tier; by default it is taken when the planned
+ * work per CTA is large (its CTAs start and drain a little later but process
+ * far tokens a little faster).  The environment variable FKV_QK_PATH=mma or
+ * FKV_QK_PATH=tcgen05 forces either path where the shape allows it. */
 int fkv_decode_qk_path(const FkvDecodeShape* s, const uint8_t* far_k);
 
 /* TurboQuant far tier, scores directly on codes.  Replaces
