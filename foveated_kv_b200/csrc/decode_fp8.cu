@@ -833,6 +833,7 @@ __device__ __forceinline__ void turbo_tile(const uint8_t* __restrict__ sgn,
 // records, through double-buffered bulk copies (TMA) of whole records for the
 // split records (bandwidth- instead of latency-bound for many splits).
 constexpr int kMaxSplits = 64;
+constexpr int kDirectMerge = 10;   // split counts merged with direct loads
 constexpr int kMergeScratch = (kMaxSplits * 40 + kMaxSplits * 8 + 8) * 4;   // bytes
 
 template <bool G>
@@ -981,6 +982,39 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, const float*
     constexpr int kMergeBatch = (kStages * Ring<D>::SLOT - BUF0) / (2 * RB);
     static_assert(RB % 16 == 0 && kMergeBatch >= 2, "merge buffers must fit in the ring");
     float* scratch = reinterpret_cast<float*>(smem);
+    if (n <= kDirectMerge) {
+        // few records: every o-vector load is issued before the scalar pass,
+        // so both share one round of latency (no bulk-copy round trip)
+        constexpr int E4 = 8 * D / kConsumerThreads / 4;
+        const int e0 = threadIdx.x * (8 * D / kConsumerThreads);
+        float4 v[kDirectMerge][E4];
+#pragma unroll
+        for (int u = 0; u < kDirectMerge; ++u)
+#pragma unroll
+            for (int j = 0; j < E4; ++j)
+                if (u < n) v[u][j] = ld4<true>(base + u * R::SIZE + R::O + e0 + 4 * j);
+        merge_heads<D, true>(p, base, n, R::SIZE, s, hg, scratch);
+        const float* wk = scratch + kMaxSplits * 40;
+        const int head = e0 / D;
+        float acc[E4 * 4];
+#pragma unroll
+        for (int x = 0; x < E4 * 4; ++x) acc[x] = 0.f;
+#pragma unroll
+        for (int u = 0; u < kDirectMerge; ++u) {
+            if (u < n) {
+                const float wgt = wk[u * 8 + head];
+#pragma unroll
+                for (int j = 0; j < E4; ++j) {
+                    acc[4 * j + 0] = fmaf(wgt, v[u][j].x, acc[4 * j + 0]);
+                    acc[4 * j + 1] = fmaf(wgt, v[u][j].y, acc[4 * j + 1]);
+                    acc[4 * j + 2] = fmaf(wgt, v[u][j].z, acc[4 * j + 2]);
+                    acc[4 * j + 3] = fmaf(wgt, v[u][j].w, acc[4 * j + 3]);
+                }
+            }
+        }
+        merge_emit<D>(p, acc, s, hg, scratch);
+        return;
+    }
     const int nb = (n + kMergeBatch - 1) / kMergeBatch;
     auto issue = [&](int bi) {
         const int cnt = min(kMergeBatch, n - bi * kMergeBatch);
