@@ -231,7 +231,7 @@ def main_seqsplit(args, rank, world, device):
     import torch
     import torch.distributed as dist
     from foveated_kv_b200 import TierConfig
-    from foveated_kv_b200.seqsplit import shard_bounds_balanced, compress_shard, decode_seqsplit
+    from foveated_kv_b200.seqsplit import shard_bounds_balanced, compress_shard, SeqSplitDecoder
     from foveated_kv_b200.synthetic import torch_workload, CONFIGS
     c = CONFIGS["c4"]
     B, Hq, Hk, D, S = c["B"], c["Hq"], c["Hk"], c["D"], c["S"]
@@ -253,17 +253,20 @@ def main_seqsplit(args, rank, world, device):
     del w
     # one GPU: the step (partial + combine kernels) is captured in a CUDA
     # graph; several GPUs: eager steps (the NCCL all-gather is not captured)
+    # prepared per-layer step: one partial call, one all-gather, one strided
+    # combine (buffers allocated once, little host work per step)
+    dec = SeqSplitDecoder(lay, off, Hq)
     graph = None
     if world == 1:
         gs = torch.cuda.Stream(device)
         with torch.cuda.stream(gs):
             for _ in range(max(args.warmup, 3)):
-                decode_seqsplit(lay, q, off)
+                dec.step(q)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=gs):
-            decode_seqsplit(lay, q, off)
-    step = graph.replay if graph is not None else (lambda: decode_seqsplit(lay, q, off))
+            dec.step(q)
+    step = graph.replay if graph is not None else (lambda: dec.step(q))
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
@@ -297,7 +300,7 @@ def main_seqsplit(args, rank, world, device):
 
     def e2e_step():
         q_dev.copy_(q_host, non_blocking=True)
-        for h, d in zip(outs_h, decode_seqsplit(lay, q_dev, off)):
+        for h, d in zip(outs_h, dec.step(q_dev)):
             h.copy_(d, non_blocking=True)
         st.synchronize()
 

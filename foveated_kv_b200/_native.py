@@ -73,6 +73,8 @@ SIGNATURES = {
     "fkv_decode_fp8_partial": (C.c_int, [C.POINTER(DecodeShape), P, P, P, P, P, P, P, P, P,
                                          P, I32, P, P, P, SZ, P]),
     "fkv_combine_partials": (C.c_int, [I32, I32, I32, P, P, C.c_float, P, P, P, P]),
+    "fkv_combine_partials_strided": (C.c_int, [I32, I32, I32, P, C.c_int64, P, C.c_int64, C.c_float,
+                                               P, P, P, P]),
     "fkv_promo_create": (P, [I32, I32, I32, I32]),
     "fkv_promo_register_archive": (C.c_int, [P, I32, C.c_char_p, C.c_char_p, I32, I32, I32,
                                              I32, P, I64]),

@@ -1499,20 +1499,22 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
     merge_splits<D>(p, base, p.splits, s, hg, smem, reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR));
 }
 
+// shard k's record n at parts + k * prs + n * (D + 4), its argmax at
+// args + k * ars + n (prs / ars: element strides between the shards' blocks)
 template <int D>
-__global__ void combine_kernel(int P, int N, const float* __restrict__ parts,
-                               const int32_t* __restrict__ args, float margin,
+__global__ void combine_kernel(int P, int N, const float* __restrict__ parts, int64_t prs,
+                               const int32_t* __restrict__ args, int64_t ars, float margin,
                                uint16_t* __restrict__ out, int32_t* __restrict__ flags,
                                int32_t* __restrict__ tokens) {
     const int n = blockIdx.x;
     const int64_t rs = D + 4;
     float M = -INFINITY;
-    for (int k = 0; k < P; ++k) M = fmaxf(M, parts[((int64_t)k * N + n) * rs]);
+    for (int k = 0; k < P; ++k) M = fmaxf(M, parts[k * prs + n * rs]);
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         float L = 0.f, acc = 0.f;
         if (M != -INFINITY) {
             for (int k = 0; k < P; ++k) {
-                const float* rec = parts + ((int64_t)k * N + n) * rs;
+                const float* rec = parts + k * prs + n * rs;
                 if (rec[0] == -INFINITY) continue;
                 const float wgt = exp2f((rec[0] - M) * kLog2e);
                 L = fmaf(wgt, rec[1], L);
@@ -1525,11 +1527,11 @@ __global__ void combine_kernel(int P, int N, const float* __restrict__ parts,
         float mn = INFINITY, mf = -INFINITY;
         int af = -1;
         for (int k = 0; k < P; ++k) {
-            const float* rec = parts + ((int64_t)k * N + n) * rs;
+            const float* rec = parts + k * prs + n * rs;
             mn = fminf(mn, rec[2]);
             if (rec[3] > mf) {   // shard order: first shard with the strict max wins
                 mf = rec[3];
-                af = args[(int64_t)k * N + n];
+                af = args[k * ars + n];
             }
         }
         flags[n] = (mf > mn + margin) ? 1 : 0;
@@ -1995,21 +1997,32 @@ int fkv_decode_fp8_partial(const FkvDecodeShape* sh, const uint16_t* near_k,
     return launch(sh, p, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
-int fkv_combine_partials(int32_t P, int32_t N, int32_t D, const float* parts,
-                         const int32_t* part_args, float spike_margin, uint16_t* out,
-                         int32_t* flags, int32_t* tokens, void* stream) {
+int fkv_combine_partials_strided(int32_t P, int32_t N, int32_t D, const float* parts,
+                                 int64_t part_rank_stride, const int32_t* part_args,
+                                 int64_t arg_rank_stride, float spike_margin, uint16_t* out,
+                                 int32_t* flags, int32_t* tokens, void* stream) {
     fkv::clear_error();
     FKV_REQUIRE(P > 0 && N > 0, FKV_ERR_INVALID, "P=%d N=%d must be positive", P, N);
     FKV_REQUIRE(D == 64 || D == 128, FKV_ERR_UNSUPPORTED, "head dim %d unsupported", D);
     FKV_REQUIRE(parts && part_args && out && flags && tokens, FKV_ERR_INVALID, "NULL argument");
+    FKV_REQUIRE(part_rank_stride >= (int64_t)N * (D + 4) && arg_rank_stride >= N, FKV_ERR_INVALID,
+                "rank strides %lld / %lld smaller than one shard's records",
+                (long long)part_rank_stride, (long long)arg_rank_stride);
     if (D == 128)
-        combine_kernel<128><<<N, 128, 0, (cudaStream_t)stream>>>(P, N, parts, part_args,
-                                                                 spike_margin, out, flags, tokens);
+        combine_kernel<128><<<N, 128, 0, (cudaStream_t)stream>>>(
+            P, N, parts, part_rank_stride, part_args, arg_rank_stride, spike_margin, out, flags, tokens);
     else
-        combine_kernel<64><<<N, 64, 0, (cudaStream_t)stream>>>(P, N, parts, part_args,
-                                                               spike_margin, out, flags, tokens);
+        combine_kernel<64><<<N, 64, 0, (cudaStream_t)stream>>>(
+            P, N, parts, part_rank_stride, part_args, arg_rank_stride, spike_margin, out, flags, tokens);
     FKV_LAUNCH_CHECK();
     return FKV_OK;
+}
+
+int fkv_combine_partials(int32_t P, int32_t N, int32_t D, const float* parts,
+                         const int32_t* part_args, float spike_margin, uint16_t* out,
+                         int32_t* flags, int32_t* tokens, void* stream) {
+    return fkv_combine_partials_strided(P, N, D, parts, (int64_t)N * (D + 4), part_args, N,
+                                        spike_margin, out, flags, tokens, stream);
 }
 
 }  // extern "C"

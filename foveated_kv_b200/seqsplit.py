@@ -199,3 +199,72 @@ def decode_seqsplit(layer: FoveatedLayer, q: torch.Tensor, far_offset: int, grou
     parts, args = gather_partials(part, arg, group)
     out, fl, tk = combine(parts, args, layer.spike_margin)
     return out.view(B, Hq, 1, D), fl.view(B, Hq), tk.view(B, Hq)
+
+
+class SeqSplitDecoder:
+    """Repeated sequence-split decode steps of one layer shard.
+
+    The decode shape, a workspace, the [records | argmax] buffer, the buffer
+    that receives every rank's copy of it and the outputs are prepared once;
+    a step is then one partial-kernel call, one all-gather and one combine
+    call that reads the gathered blocks in place
+    (fkv_combine_partials_strided).  Little host work per step matters when
+    several ranks share a host's cores.  The tensors step() returns are
+    overwritten by the next step: copy them to keep them."""
+
+    def __init__(self, layer: FoveatedLayer, far_offset: int, Hq: int, group=None):
+        self.lib = _native.load()
+        self.layer, self.far_offset, self.group = layer, int(far_offset), group
+        self.P = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
+        self.B, self.Hq, self.D = layer.B, Hq, layer.D
+        self.N = self.B * Hq
+        self.rec = self.N * (self.D + 4) + self.N          # floats per rank block
+        dev = layer.device
+        self.sh = _native.DecodeShape()
+        self.ws = None
+        self._refresh_shape()
+        self.flat = torch.empty((self.rec,), dtype=torch.float32, device=dev)
+        self.gathered = (torch.empty((self.P * self.rec,), dtype=torch.float32, device=dev)
+                         if self.P > 1 else self.flat)
+        self.qbuf = torch.empty((self.B, Hq, self.D), dtype=F16, device=dev)
+        self.out = torch.empty((self.N, self.D), dtype=F16, device=dev)
+        self.flags = torch.empty((self.N,), dtype=I32, device=dev)
+        self.tokens = torch.empty((self.N,), dtype=I32, device=dev)
+
+    def _refresh_shape(self):
+        src = self.layer._fill_shape(self.Hq, self.layer.spike_margin)
+        key = (src.n_dec, src.dec_stride)
+        C.memmove(C.addressof(self.sh), C.addressof(src), C.sizeof(self.sh))
+        if self.ws is None or key != self._ws_key:
+            need = self.lib.fkv_decode_workspace_bytes(C.byref(self.sh)) + 256
+            if self.ws is None or self.ws.numel() < need:
+                self.ws = torch.zeros((need,), dtype=torch.uint8, device=self.layer.device)
+            self._ws_key = key
+
+    def step(self, q: torch.Tensor):
+        """One decode step: returns (out (B, Hq, 1, D), flags (B, Hq), tokens (B, Hq))."""
+        lay, lib, N, D = self.layer, self.lib, self.N, self.D
+        if (lay._n_dec, lay._dec_k.shape[2]) != self._ws_key:
+            self._refresh_shape()
+        qq = q.reshape(self.B, self.Hq, D)
+        if qq.dtype != F16 or not qq.is_contiguous():
+            self.qbuf.copy_(qq)
+            qq = self.qbuf
+        dk = lay._dec_k if lay.n_decode else None
+        dv = lay._dec_v if lay.n_decode else None
+        st = _stream(lay.device)
+        base = self.flat.data_ptr()
+        _native.check(lib.fkv_decode_fp8_partial(
+            C.byref(self.sh), _p(lay.near_k), _p(lay.near_v), _p(lay.near_valid), _p(lay.far_k),
+            _p(lay.far_v), _p(lay.far_v_scale), _p(lay.far_v_zero), _p(qq), _p(dk), _p(dv),
+            self.far_offset, base, base + N * (D + 4) * 4, self.ws.data_ptr(), self.ws.numel(), st),
+            "fkv_decode_fp8_partial")
+        if self.P > 1:
+            dist.all_gather_into_tensor(self.gathered, self.flat, group=self.group)
+        g = self.gathered.data_ptr()
+        _native.check(lib.fkv_combine_partials_strided(
+            self.P, N, D, g, self.rec, g + N * (D + 4) * 4, self.rec, float(lay.spike_margin),
+            self.out.data_ptr(), self.flags.data_ptr(), self.tokens.data_ptr(), st),
+            "fkv_combine_partials_strided")
+        return (self.out.view(self.B, self.Hq, 1, D), self.flags.view(self.B, self.Hq),
+                self.tokens.view(self.B, self.Hq))

@@ -221,6 +221,16 @@ int fkv_combine_partials(int32_t P, int32_t N, int32_t D, const float* parts,
                          const int32_t* part_args, float spike_margin, uint16_t* out,
                          int32_t* flags, int32_t* tokens, void* stream);
 
+/* Same merge reading each shard's block in place (no counterpart in the
+ * reference): shard k's records start at parts + k * part_rank_stride and its
+ * argmax values at part_args + k * arg_rank_stride (element strides, at
+ * least N * (D+4) and N).  Lets a caller gather every shard's [records |
+ * argmax] buffer with one collective and merge it without repacking. */
+int fkv_combine_partials_strided(int32_t P, int32_t N, int32_t D, const float* parts,
+                                 int64_t part_rank_stride, const int32_t* part_args,
+                                 int64_t arg_rank_stride, float spike_margin, uint16_t* out,
+                                 int32_t* flags, int32_t* tokens, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Spike drain + promotion                                                  */
 /* ------------------------------------------------------------------------ */

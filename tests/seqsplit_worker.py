@@ -9,7 +9,8 @@ import torch.distributed as dist
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 from foveated_kv_b200 import TierConfig, compress_layer  # noqa: E402
-from foveated_kv_b200.seqsplit import shard_bounds, compress_shard, decode_seqsplit  # noqa: E402
+from foveated_kv_b200.seqsplit import (shard_bounds, compress_shard, decode_seqsplit,  # noqa: E402
+                                       SeqSplitDecoder)
 from foveated_kv_b200.synthetic import numpy_workload  # noqa: E402
 
 
@@ -25,7 +26,11 @@ def main():
     lo, hi = shard_bounds(S, rank, world)
     lay, off = compress_shard(t["k"][:, :, lo:hi], t["v"][:, :, lo:hi], S, lo, cfg)
     out, fl, tk = decode_seqsplit(lay, t["q"], off)
+    dec = SeqSplitDecoder(lay, off, Hq)
+    o2, f2, t2 = dec.step(t["q"])
+    o2, f2, t2 = dec.step(t["q"])          # second step re-uses every buffer
     torch.cuda.synchronize()
+    assert torch.equal(o2, out) and torch.equal(f2, fl) and torch.equal(t2, tk)
     if rank == 0:
         full = compress_layer(t["k"], t["v"], cfg)
         ro, rf, rt = full.attend_fused_with_spikes(t["q"])

@@ -129,6 +129,15 @@ def test_partials_on_one_gpu_equal_unsplit(P, path, monkeypatch):
         parts.append(pa); args.append(ar)
     out, fl, tk = combine(torch.stack(parts), torch.stack(args), 0.5)
     torch.cuda.synchronize()
+    if P == 1:
+        # the prepared step (one buffer, strided combine) gives the same result
+        from foveated_kv_b200.seqsplit import SeqSplitDecoder
+        dec = SeqSplitDecoder(lay, off, Hq)
+        for _ in range(2):
+            o2, f2, t2 = dec.step(t["q"])
+            torch.cuda.synchronize()
+            assert torch.equal(o2.reshape(out.shape), out)
+            assert torch.equal(f2.reshape(-1), fl) and torch.equal(t2.reshape(-1), tk)
     assert (out.float() - ref_out.float().reshape(out.shape)).abs().max().item() < 2e-3
     assert torch.equal(fl.cpu(), ref_fl.reshape(-1).cpu())
     assert torch.equal(tk.cpu(), ref_tk.reshape(-1).cpu())
