@@ -63,7 +63,7 @@ struct DecodeParams {
     const float* turbo_pi;
     const float* turbo_s;
     float qjl_coef;
-    int B, Hq, Hk, G, HG, Np, F, n_dec, dec_stride, splits, chunk;
+    int B, Hq, Hk, G, HG, Np, F, n_dec, dec_stride, splits;
     int near_w, far_w;    // cost units of an fp16 near / decode token and of a far token
     float margin, qscale;
 };
@@ -1853,7 +1853,7 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     FKV_REQUIRE(aligned16(workspace), FKV_ERR_INVALID, "workspace must be 16-byte aligned");
     p.B = sh->B; p.Hq = sh->Hq; p.Hk = sh->Hk; p.G = sh->Hq / sh->Hk; p.HG = pl.HG;
     p.Np = sh->n_near_alloc; p.F = sh->n_far; p.n_dec = sh->n_dec; p.dec_stride = sh->dec_stride;
-    p.splits = pl.splits; p.chunk = pl.chunk; p.near_w = pl.near_w; p.far_w = pl.far_w; p.margin = sh->spike_margin;
+    p.splits = pl.splits; p.near_w = pl.near_w; p.far_w = pl.far_w; p.margin = sh->spike_margin;
     p.qscale = (float)(1.0 / sqrt((double)sh->D));   // same f32 constant as the host oracle
     // split counters at the front, split records at the back: a workspace
     // shared by calls of different shapes keeps every counter at zero as long
