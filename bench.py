@@ -319,6 +319,11 @@ def main_seqsplit(args, rank, world, device):
     peak = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"] \
         if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else 6650.0
     achieved = alg_total / world / (ms * 1e-3) / 1e9
+    c4_traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            c4_traffic = json.load(f).get("c4", {}).get("traffic_bytes_per_launch")
     if rank == 0:
         print(json.dumps({
             "metric": METRIC_FMT.format("c4"), "value": B / (N_LAYERS * ms * 1e-3),
@@ -334,7 +339,8 @@ def main_seqsplit(args, rank, world, device):
             "us_per_layer": ms * 1e3, "compress_ms": compress_ms,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "algorithmic_bytes_per_launch": alg_total / world,
-                         "traffic": None, "note": "per-GPU bytes / step time (includes all-gather)"},
+                         "traffic": c4_traffic if world == 1 else None,
+                         "note": "per-GPU bytes / step time (includes all-gather)"},
             "e2e": {"value": B / (N_LAYERS * ms_e2e * 1e-3), "unit": "tokens/s",
                     "ms_per_step": ms_e2e, "h2d_bytes_per_step": q.numel() * 2,
                     "d2h_bytes_per_step": B * Hq * (2 * D + 8)},
