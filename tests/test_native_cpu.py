@@ -80,3 +80,21 @@ def test_shape_limits_rejected_before_any_cuda_call():
     L = _native.TierLayout()
     assert lib.fkv_compress_fp8(C.byref(L), 1, 1, 96, None, None, 0, None, None, 0,
                                 *([None] * 8), None) == -2          # head dim 96 unsupported
+
+
+def test_strided_combine_and_path_query_validate_without_gpu():
+    lib = _native.load()
+    dummy = C.c_void_p(16)          # never dereferenced: validation fails first
+    # rank strides smaller than one shard's records are rejected
+    rc = lib.fkv_combine_partials_strided(2, 4, 128, dummy, 4 * 132 - 1, dummy, 4, 0.5,
+                                          dummy, dummy, dummy, None)
+    assert rc == -1 and b"stride" in lib.fkv_last_error()
+    assert lib.fkv_combine_partials_strided(2, 4, 96, dummy, 10**6, dummy, 10**6, 0.5,
+                                            dummy, dummy, dummy, None) == -2
+    assert lib.fkv_combine_partials_strided(0, 4, 128, dummy, 10**6, dummy, 10**6, 0.5,
+                                            dummy, dummy, dummy, None) == -1
+    # the q.K path query validates the shape first
+    sh = _native.DecodeShape(B=1, Hq=6, Hk=4, D=128)
+    assert lib.fkv_decode_qk_path(C.byref(sh), None) == -1
+    sh = _native.DecodeShape(B=1, Hq=8, Hk=2, D=64, n_far=100)
+    assert lib.fkv_decode_qk_path(C.byref(sh), None) == 0      # D = 64: mma.sync path only
