@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--cpu-sample-seqs", type=int, default=1)
     ap.add_argument("--batch", type=int, default=0, help="override sequences per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sdpa", action="store_true", help="skip the fp16 SDPA comparison")
+    ap.add_argument("--sdpa-flashinfer", action="store_true",
+                    help="also time flashinfer's decode (JIT-compiles on first use)")
     return ap.parse_args()
 
 
@@ -107,7 +110,7 @@ def algorithmic_bytes(B, Hq, Hk, D, near_valid_sum, F, n_dec, turbo=False):
 def build_layer(cfgname, seed, device, batch=0):
     import torch
     from foveated_kv_b200 import TierConfig, compress_layer
-    from foveated_kv_b200.synthetic import torch_workload, CONFIGS
+    from foveated_kv_b200.synthetic import torch_workload, inject_spikes_torch, CONFIGS
     c = dict(CONFIGS[cfgname])
     if batch:
         c["B"] = batch
@@ -116,10 +119,16 @@ def build_layer(cfgname, seed, device, batch=0):
                      v_group=c["v_group"], compress_method=c["compress_method"],
                      select=c["select"], spike_margin=0.5)
     if cfgname == "c3":
-        inject_spikes(w, cfg, seed)
+        inject_spikes_torch(w, cfg.tier_boundaries(c["S"]), seed)
     # importance selection (c0) scores tokens with the seeded query
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
     lay = compress_layer(w["k"], w["v"], cfg,
                          query=w["q"] if c["select"] == "importance" else None)
+    e1.record()
+    torch.cuda.synchronize()
+    lay.compress_ms = e0.elapsed_time(e1)
     for i in range(c["n_dec"]):
         lay.add_token(w["dec_k"][:, :, i:i + 1], w["dec_v"][:, :, i:i + 1])
     q = w["q"]
@@ -128,61 +137,70 @@ def build_layer(cfgname, seed, device, batch=0):
     return c, cfg, lay, q
 
 
-def inject_spikes(w, cfg, seed, frac=0.01):
-    """1% of far tokens per (b, kv head): key = 3 sigma * sqrt(D) along the
-    unit mean query of the GQA group, so they score far above min_near."""
-    import torch
-    k, q = w["k"], w["q"]
-    B, Hk, S, D = k.shape
-    G = q.shape[1] // Hk
-    tb = cfg.tier_boundaries(S)
-    F = tb["far_count"]
-    n = max(1, int(F * frac))
-    g = torch.Generator(device=k.device)
-    g.manual_seed(seed + 1)
-    pos = tb["mid_start"] + torch.randint(0, F, (B, Hk, n), generator=g, device=k.device)
-    qm = q.float().reshape(B, Hk, G, D).mean(2)
-    qm = qm / qm.norm(dim=-1, keepdim=True)
-    val = (3.0 * D ** 0.5 * qm).to(k.dtype)[:, :, None, :].expand(B, Hk, n, D)
-    k.scatter_(2, pos[..., None].expand(B, Hk, n, D), val)
-
-
 class CpuArm:
-    """The CPU oracle (dequantise-then-attend, NumPy) on `seqs` sequences of
-    the same workload; built once, timed per call."""
+    """The reference's CPU path on `seqs` sequences of the same workload:
+    ``reference_attend_f32`` (mlx_foveated.py:239-278 in its own precision:
+    fp8 -> fp16 table lookup, INT4 dequant in fp16 arithmetic, fp32 softmax
+    attention), the (b, kv head) streams on a pool of `threads` host threads
+    with single-threaded BLAS.  The tiers are built once by the oracle's
+    compress (itself timed once as the CPU compress pass)."""
 
-    def __init__(self, cfgname, seqs):
+    def __init__(self, cfgname, seqs, threads=None):
         from oracle import fkv_oracle as O
-        from foveated_kv_b200.synthetic import numpy_workload, CONFIGS
+        from foveated_kv_b200.synthetic import numpy_workload, inject_spikes_np, CONFIGS
         self.O = O
         c = CONFIGS[cfgname]
         self.seqs = min(seqs, c["B"])
         self.c, self.name = c, cfgname
+        self.threads = threads or len(os.sched_getaffinity(0))
         self.w = numpy_workload(7, self.seqs, c["Hk"], c["Hq"], c["S"], c["D"], c["n_dec"])
-        self.lay = O.compress_layer(self.w["k"], self.w["v"], dict(
-            near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
-            v_group=c["v_group"], compress_method=c["compress_method"], select=c["select"]),
-            q_obs=self.w["q"] if c["select"] == "importance" else None)
-
-    def run(self):
+        tcfg = dict(near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
+                    v_group=c["v_group"], compress_method=c["compress_method"], select=c["select"])
+        if cfgname == "c3":
+            inject_spikes_np(self.w, O.tier_boundaries(c["S"], c["near_pct"], c["n_sinks"],
+                                                       c["window_size"]), 7)
         t0 = time.perf_counter()
-        self.O.decode_attend(self.lay, self.w["q"], self.w["dec_k"], self.w["dec_v"], 0.5)
+        self.lay = O.compress_layer(self.w["k"], self.w["v"], tcfg,
+                                    q_obs=self.w["q"] if c["select"] == "importance" else None)
+        self.compress_s = time.perf_counter() - t0
+        self.turbo = c["compress_method"] == "turbo"
+
+    def run(self, threads=None):
+        from threadpoolctl import threadpool_limits
+        th = threads or self.threads
+        t0 = time.perf_counter()
+        with threadpool_limits(1):
+            if self.turbo:   # no separate reference-precision turbo path: the oracle's
+                self.O.decode_attend(self.lay, self.w["q"], self.w["dec_k"], self.w["dec_v"], 0.5)
+            else:
+                self.O.reference_attend_f32(self.lay, self.w["q"], self.w["dec_k"],
+                                            self.w["dec_v"], threads=th)
         return time.perf_counter() - t0
 
-    def describe(self, dt):
-        cores = len(os.sched_getaffinity(0))
-        return {"value": self.seqs / (N_LAYERS * dt), "unit": "tokens/s", "cores": cores,
-                "kind": "port",
-                "sample": f"{self.seqs} of {self.c['B']} sequences of {self.name}, one layer, "
-                          f"oracle decode_attend (NumPy, BLAS threads={cores}), "
-                          f"{dt * 1e3:.1f} ms/layer"}
+    def describe(self, dt, dt1=None):
+        what = ("oracle decode_attend (NumPy fp64; turbo)" if self.turbo else
+                "reference attend in its own precision (fp8->fp16 LUT, INT4 dequant in fp16, "
+                "fp32 softmax attention; NumPy)")
+        d = {"value": self.seqs / (N_LAYERS * dt), "unit": "tokens/s", "cores": self.threads,
+             "kind": "port",
+             "sample": f"{self.seqs} of {self.c['B']} sequences of {self.name}, one layer, {what}, "
+                       f"{self.threads} threads: {dt * 1e3:.1f} ms/layer",
+             "ms_per_layer": dt * 1e3,
+             "compress_ms_per_layer": self.compress_s * 1e3,
+             "compress_note": "oracle compress_layer (NumPy restatement of _assign_and_build_layer, "
+                              "mlx_foveated.py:799-944) on the same sample, 1 thread"}
+        if dt1 is not None:
+            d["value_1thread"] = self.seqs / (N_LAYERS * dt1)
+            d["ms_per_layer_1thread"] = dt1 * 1e3
+        return d
 
 
 def cpu_baseline(cfgname, seqs, reps=3):
     arm = CpuArm(cfgname, seqs)
     arm.run()
     dt = statistics.median(arm.run() for _ in range(reps))
-    return arm.describe(dt)
+    dt1 = statistics.median(arm.run(threads=1) for _ in range(2))
+    return arm.describe(dt, dt1)
 
 
 def reference_arm(args, rank, world):
@@ -199,14 +217,101 @@ def reference_arm(args, rank, world):
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": args.config, "sample_seqs": arm.seqs},
+            "config": {"workload": args.config, "sample_seqs": arm.seqs,
+                       "same_config": arm.seqs == arm.c["B"],
+                       "normalisation": "per sequence: value = sample sequences / (32 x layer time)"},
             "cpu_baseline": d,
             "e2e": {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
-            "note": "reference CPU path = NumPy restatement of mlx_foveated.attend "
-                    "(MLX/Metal cannot run on Linux/B200)"}
+            "note": "reference CPU path = NumPy restatement of mlx_foveated.attend in its own "
+                    "precision (MLX/Metal cannot run on Linux/B200); a bounded sample of the "
+                    "workload (seed 7, with the config's injected spikes), normalised per sequence"}
     print(json.dumps(line), flush=True)
 
+
+def sdpa_fp16_baseline(c, device, steps, warmup, layers_bytes=4e9, flashinfer=False):
+    """fp16 full-cache decode attention of the same shape (B, Hq / Hk, D, S):
+    the denominator of the north-star target t_fused <= t_sdpa / ratio.  Times
+    each available library path (torch SDPA backends, flash-attn's kvcache
+    decode, optionally flashinfer) over enough distinct layers to exceed L2,
+    in a CUDA graph, and reports the fastest.  Library code: a baseline, not
+    the product path."""
+    import torch
+    import torch.nn.functional as Fn
+    B, Hq, Hk, D, S = c["B"], c["Hq"], c["Hk"], c["D"], c["S"]
+    per_layer = B * Hk * S * D * 4
+    L = max(1, min(32, int(layers_bytes // per_layer)))
+    g = torch.Generator(device=device)
+    g.manual_seed(5)
+    q = torch.randn((B, Hq, 1, D), generator=g, device=device, dtype=torch.float16)
+    res = {}
+
+    def time_graph(fn):
+        st = torch.cuda.Stream(device)
+        with torch.cuda.stream(st):
+            for _ in range(3):
+                fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=st):
+            fn()
+        for _ in range(max(warmup, 3)):
+            gr.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e3 / (steps * L)     # us per layer
+
+    # (B, Hk, S, D) caches for torch SDPA
+    ks = [torch.randn((B, Hk, S, D), generator=g, device=device, dtype=torch.float16) for _ in range(L)]
+    vs = [torch.randn((B, Hk, S, D), generator=g, device=device, dtype=torch.float16) for _ in range(L)]
+    outs = [torch.empty((B, Hq, 1, D), device=device, dtype=torch.float16) for _ in range(L)]
+    from torch.nn.attention import sdpa_kernel, SDPBackend
+    for name, be in (("torch_sdpa_flash", SDPBackend.FLASH_ATTENTION),
+                     ("torch_sdpa_efficient", SDPBackend.EFFICIENT_ATTENTION),
+                     ("torch_sdpa_cudnn", SDPBackend.CUDNN_ATTENTION)):
+        try:
+            def fn(be=be):
+                with sdpa_kernel([be]):
+                    for i in range(L):
+                        outs[i].copy_(Fn.scaled_dot_product_attention(q, ks[i], vs[i],
+                                                                      enable_gqa=Hq != Hk))
+            res[name] = time_graph(fn)
+        except Exception as e:   # backend unavailable for this shape / device
+            res[name] = f"unavailable: {type(e).__name__}: {str(e)[:120]}"
+    del ks, vs
+    torch.cuda.empty_cache()
+    # (B, S, Hk, D) caches for flash-attn's decode kernel
+    try:
+        from flash_attn import flash_attn_with_kvcache
+        kc = [torch.randn((B, S, Hk, D), generator=g, device=device, dtype=torch.float16) for _ in range(L)]
+        vc = [torch.randn((B, S, Hk, D), generator=g, device=device, dtype=torch.float16) for _ in range(L)]
+        qf = q.transpose(1, 2).contiguous()          # (B, 1, Hq, D)
+
+        def fa():
+            for i in range(L):
+                flash_attn_with_kvcache(qf, kc[i], vc[i])
+        res["flash_attn2_kvcache"] = time_graph(fa)
+        if flashinfer and B == 1:
+            import flashinfer as fi
+            q2 = q[0, :, 0].contiguous()
+
+            def fib():
+                for i in range(L):
+                    fi.single_decode_with_kv_cache(q2, kc[i][0], vc[i][0], kv_layout="NHD")
+            res["flashinfer_single_decode"] = time_graph(fib)
+        del kc, vc
+    except Exception as e:
+        res.setdefault("flash_attn2_kvcache", f"unavailable: {type(e).__name__}: {str(e)[:120]}")
+    torch.cuda.empty_cache()
+    times = {k: v for k, v in res.items() if isinstance(v, float)}
+    best = min(times, key=times.get) if times else None
+    return {"us_per_layer": times.get(best) if best else None, "impl": best, "all": res,
+            "layers_per_graph": L, "fp16_bytes_per_layer": per_layer + B * Hq * D * 4}
 
 
 def qk_path_name(lay, Hq: int) -> str:
@@ -453,6 +558,20 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.config, args.cpu_sample_seqs)
+    compress_ms = layers[0].compress_ms
+    del layers, outs, graph
+    torch.cuda.empty_cache()
+    sdpa = None
+    if not args.no_sdpa and rank == 0:
+        c_full = dict(c)
+        sdpa = sdpa_fp16_baseline(c_full, device, min(args.steps, 100), args.warmup,
+                                  flashinfer=args.sdpa_flashinfer)
+        if sdpa["us_per_layer"]:
+            ratio = sdpa["fp16_bytes_per_layer"] / alg
+            sdpa.update(t_fused_us=ms * 1e3, speedup=sdpa["us_per_layer"] / (ms * 1e3),
+                        compression_ratio=ratio,
+                        target="t_fused <= t_sdpa / compression_ratio",
+                        target_met=ms * 1e3 <= sdpa["us_per_layer"] / ratio)
 
     peaks_path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(peaks_path):
@@ -489,6 +608,10 @@ def main():
                          "traffic_source": "ncu dram__bytes_read+write per launch (profiles/)"},
             "e2e": {"value": world * B / (N_LAYERS * ms_e2e * 1e-3), "unit": "tokens/s",
                     "ms_per_step": ms_e2e, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "compress_ms_per_layer": compress_ms,
+            "compress_gbs": (lay.memory_bytes()["total_with_archive"] +
+                             B * Hk * c["S"] * D * 4) / (compress_ms * 1e-3) / 1e9,
+            "sdpa_fp16": sdpa,
             "gpu_launches": args.steps * n_layers,
             "layers_per_graph": n_layers,
             "clocks": clk.summary(),

@@ -40,7 +40,12 @@ class DecodeShape(C.Structure):
     _fields_ = [("B", C.c_int32), ("Hq", C.c_int32), ("Hk", C.c_int32), ("D", C.c_int32),
                 ("n_near_alloc", C.c_int32), ("n_far", C.c_int32), ("n_dec", C.c_int32),
                 ("dec_stride", C.c_int32), ("v_group", C.c_int32), ("num_splits", C.c_int32),
-                ("spike_margin", C.c_float), ("qjl_coef", C.c_float)]
+                ("spike_margin", C.c_float), ("qjl_coef", C.c_float), ("wait_limit", C.c_int32),
+                ("test_flags", C.c_int32)]
+
+
+FKV_TEST_STALL = 1
+FKV_ERR_TIMEOUT = -4
 
 
 P = C.c_void_p
@@ -64,6 +69,8 @@ SIGNATURES = {
                                      P, P, P, P, P, P, P, P, P, P, P, P, P, P, P]),
     "fkv_decode_workspace_bytes": (SZ, [C.POINTER(DecodeShape)]),
     "fkv_decode_qk_path": (C.c_int, [C.POINTER(DecodeShape), P]),
+    "fkv_decode_status": (C.c_int, [P, C.POINTER(I32), I32, P]),
+    "fkv_decode_noalloc_status": (C.c_int, [C.POINTER(I32), P]),
     "fkv_decode_fp8": (C.c_int, [C.POINTER(DecodeShape), P, P, P, P, P, P, P, P, P, P, P, P,
                                  P, P, SZ, P]),
     "fkv_decode_turbo": (C.c_int, [C.POINTER(DecodeShape), P, P, P, P, P, P, P, P, P, P, P,

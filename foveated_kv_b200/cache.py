@@ -52,6 +52,20 @@ class _Workspace:
         return buf
 
 
+def workspace_status(device: torch.device, clear: bool = True) -> int:
+    """Kernel status word of the shared decode workspace of (device, current
+    stream): 0 = every launch since the last clear completed its waits."""
+    key = (device.index, _stream(device))
+    buf = _Workspace._pool.get(key, (None, 0))[0]
+    if buf is None:
+        return 0
+    lib = _native.load()
+    st = C.c_int32(0)
+    _native.check(lib.fkv_decode_status(buf.data_ptr(), C.byref(st), int(clear), key[1]),
+                  "fkv_decode_status")
+    return int(st.value)
+
+
 class FoveatedLayer:
     """Single-layer two-tier store (near fp16 + far fp8/INT4 or TurboQuant).
 
@@ -157,6 +171,8 @@ class FoveatedLayer:
         s.num_splits = 0
         s.spike_margin = margin
         s.qjl_coef = self.qjl_coef
+        s.wait_limit = 0
+        s.test_flags = 0
         return s
 
     def attend_fused_with_spikes(self, query: torch.Tensor, spike_margin: Optional[float] = None,
@@ -204,6 +220,20 @@ class FoveatedLayer:
                 _p(dk), _p(dv), _p(out), _p(flags), _p(tokens), ws.data_ptr(), ws.numel(), st)
             _native.check(rc, "fkv_decode_fp8")
         return out, flags, tokens
+
+    def decode_status(self, clear: bool = True) -> int:
+        """Status word of the fused decode calls issued on the current stream
+        since it was last cleared: 0, or -4 (FKV_ERR_TIMEOUT) when a bounded
+        wait inside a launch expired (that launch's outputs are not valid).
+        Waits for the stream."""
+        return workspace_status(self.device, clear)
+
+    def check_decode(self) -> None:
+        """Raise FkvNativeError if a decode launch on the current stream timed out."""
+        st = self.decode_status(clear=True)
+        if st != 0:
+            raise _native.FkvNativeError(
+                f"fused decode kernel reported status {st} ({_native.FKV_ERRORS.get(st, st)})")
 
     def attend_fused(self, query: torch.Tensor) -> torch.Tensor:
         return self.attend_fused_with_spikes(query)[0]

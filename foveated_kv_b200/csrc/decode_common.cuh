@@ -222,9 +222,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for phase `parity` of `bar` with an iteration limit; false = gave up.
+// kWaitLimit is the default limit of the progress waits (a caller may lower
+// it per launch) and the fixed limit of the clean-up waits that let copies
+// and tensor-core work in flight finish before a CTA exits.
 constexpr uint32_t kWaitLimit = 1u << 26;
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kWaitLimit; ++i)
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
+                                          uint32_t limit = kWaitLimit) {
+    for (uint32_t i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }

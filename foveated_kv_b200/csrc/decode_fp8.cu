@@ -53,6 +53,8 @@ struct DecodeParams {
     float* ws;            // split records
     int32_t* tickets;     // one counter per (stream, head group)
     int32_t* status;      // sticky kernel status word (0 = ok)
+    uint32_t wait_limit;  // iteration limit of the progress waits
+    int test_stall;       // 1: consumers first wait on a barrier nothing completes
     // TurboQuant far tier (far_k = 2-bit key codes, far_v = 2-bit value codes,
     // v_scale = per-32-dim value scales)
     const uint8_t* k_signs;
@@ -222,7 +224,8 @@ struct Ring {
     static constexpr int TSUM = QOFF + (VG == kTurbo ? 3 : 1) * QFRAG;   // turbo row sums
     static constexpr int BAROFF = TSUM + (VG == kTurbo ? 64 : 0);        // mbarriers
     static constexpr int MERGEBAR = BAROFF + 2 * kStages * 8;          // 2 split-merge barriers
-    static constexpr int BYTES = MERGEBAR + 2 * 8;   // (+1024 at launch: base alignment slack)
+    static constexpr int STALLBAR = MERGEBAR + 2 * 8;                  // never completed (test hook)
+    static constexpr int BYTES = STALLBAR + 8;   // (+1024 at launch: base alignment slack)
 };
 
 // Extra shared memory of the tensor-core far path (placed after the ring's
@@ -565,12 +568,13 @@ __device__ __forceinline__ bool far_tiles_um(uint8_t* __restrict__ kbuf,
                                              const uint8_t* __restrict__ vbuf, const int (&u0)[NT],
                                              int cnt, int gbase, int lane, int w, uint32_t taddr,
                                              float escale, uint64_t* mmab, uint32_t parity,
-                                             const uint32_t (&sz)[NT][4], WarpState<D>& st) {
+                                             uint32_t limit, const uint32_t (&sz)[NT][4],
+                                             WarpState<D>& st) {
     constexpr int VWN = (D / 16 + 3) / 4;
     const int r = lane >> 2, c = lane & 3;
     uint32_t vr[NT][4][VWN];
     load_far_v<D, NT>(vbuf, u0, cnt, lane, vr);   // V loads overlap the MMA wait
-    if (!mbar_wait(mmab, parity)) return false;
+    if (!mbar_wait(mmab, parity, limit)) return false;
     tc_fence_after();
     uint32_t acc[kQPieces * NH];
     if constexpr (NH == 4) tmem_ld16(taddr, acc);
@@ -1075,6 +1079,7 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
         }
         mbar_init(reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR), 1);
         mbar_init(reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR) + 1, 1);
+        mbar_init(reinterpret_cast<uint64_t*>(smem + RG::STALLBAR), 1);
         if constexpr (UM) {
             for (int i = 0; i < kStages; ++i) mbar_init(reinterpret_cast<uint64_t*>(smem + UL::MMAB) + i, 1);
             mbar_init(reinterpret_cast<uint64_t*>(smem + UL::QREADY), 3);   // TMEM + 2 piece warps
@@ -1180,7 +1185,8 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
             };
             if constexpr (!UM) {
                 for (int k = 0; k < nstage; ++k) {
-                    if (k >= kStages && !mbar_wait(empty + k % kStages, ((k / kStages) - 1) & 1)) {
+                    if (k >= kStages &&
+                        !mbar_wait(empty + k % kStages, ((k / kStages) - 1) & 1, p.wait_limit)) {
                         atomicExch(p.status, FKV_ERR_TIMEOUT);
                         break;
                     }
@@ -1235,7 +1241,7 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
                     }
                     if (prog) {
                         idle = 0;
-                    } else if (++idle > kWaitLimit) {
+                    } else if (++idle > p.wait_limit) {
                         ok = false;
                         break;
                     } else {
@@ -1303,11 +1309,20 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
     st.init();
     const int64_t srow0 = (int64_t)s * p.F;
     int failed_at = -1;
-    for (int k = 0; k < nstage; ++k) {
+    if (p.test_stall) {
+        // test hook: a wait that nothing satisfies, so the timeout path runs
+        // (error status, bounded drain of the copies in flight, normal exit)
+        // without any fault
+        if (!mbar_wait(reinterpret_cast<uint64_t*>(smem + RG::STALLBAR), 0, p.wait_limit)) {
+            atomicExch(p.status, FKV_ERR_TIMEOUT);
+            failed_at = 0;
+        }
+    }
+    for (int k = failed_at < 0 ? 0 : nstage; k < nstage; ++k) {
         const int slot = k % kStages;
         int seg, start, cnt;
         stage_at<D>(sg, k, seg, start, cnt);
-        if (!mbar_wait(full + slot, (k / kStages) & 1)) {
+        if (!mbar_wait(full + slot, (k / kStages) & 1, p.wait_limit)) {
             atomicExch(p.status, FKV_ERR_TIMEOUT);
             failed_at = k;
             break;
@@ -1332,13 +1347,13 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
                     load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
                     load_sz<D, VG>(sc, ze, u0[1], cnt, lane, sz[1]);
                     ok = far_tiles_um<D, VG, 2, NH>(kbuf, vbuf, u0, cnt, start, lane, w, ta, escale, mmab,
-                                                    par, sz, st);
+                                                    par, p.wait_limit, sz, st);
                 } else if (32 * w < cnt) {
                     const int u0[1] = {32 * w};
                     uint32_t sz[1][4];
                     load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
                     ok = far_tiles_um<D, VG, 1, NH>(kbuf, vbuf, u0, cnt, start, lane, w, ta, escale, mmab,
-                                                    par, sz, st);
+                                                    par, p.wait_limit, sz, st);
                 }
             }
             if (!ok) {
@@ -1782,6 +1797,9 @@ int validate(const FkvDecodeShape* sh) {
                     sh->dec_stride >= sh->n_dec,
                 FKV_ERR_INVALID, "bad tier sizes Np=%d F=%d n_dec=%d dec_stride=%d",
                 sh->n_near_alloc, sh->n_far, sh->n_dec, sh->dec_stride);
+    FKV_REQUIRE(sh->wait_limit >= 0 && (sh->test_flags & ~FKV_TEST_STALL) == 0, FKV_ERR_INVALID,
+                "wait_limit=%d must be >= 0 and test_flags=%d a subset of FKV_TEST_STALL",
+                sh->wait_limit, sh->test_flags);
     FKV_REQUIRE((int64_t)sh->B * sh->Hk <= 65535, FKV_ERR_UNSUPPORTED,
                 "B*Hk=%lld exceeds the grid limit 65535", (long long)sh->B * sh->Hk);
     return FKV_OK;
@@ -1855,6 +1873,8 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     p.Np = sh->n_near_alloc; p.F = sh->n_far; p.n_dec = sh->n_dec; p.dec_stride = sh->dec_stride;
     p.splits = pl.splits; p.near_w = pl.near_w; p.far_w = pl.far_w; p.margin = sh->spike_margin;
     p.qscale = (float)(1.0 / sqrt((double)sh->D));   // same f32 constant as the host oracle
+    p.wait_limit = sh->wait_limit > 0 ? (uint32_t)sh->wait_limit : kWaitLimit;
+    p.test_stall = (sh->test_flags & FKV_TEST_STALL) ? 1 : 0;
     // split counters at the front, split records at the back: a workspace
     // shared by calls of different shapes keeps every counter at zero as long
     // as it holds the largest records region plus the largest counter region.
@@ -1919,6 +1939,21 @@ size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s) {
     const Plan& ab = a.rec_bytes >= b.rec_bytes ? a : b;
     const Plan& pl = ab.rec_bytes >= c.rec_bytes ? ab : c;
     return pl.rec_bytes + pl.ticket_bytes + 256 + ((pl.qproj_bytes + 255) & ~(size_t)255) + 256;
+}
+
+int fkv_decode_status(const void* workspace, int32_t* status, int32_t clear, void* stream) {
+    fkv::clear_error();
+    FKV_REQUIRE(workspace != nullptr && status != nullptr, FKV_ERR_INVALID,
+                "fkv_decode_status: NULL argument");
+    FKV_REQUIRE(aligned16(workspace), FKV_ERR_INVALID, "workspace must be 16-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;
+    int32_t word = 0;
+    FKV_CUDA_CHECK(cudaMemcpyAsync(&word, workspace, sizeof(word), cudaMemcpyDeviceToHost, st));
+    FKV_CUDA_CHECK(cudaStreamSynchronize(st));
+    if (clear && word != 0)
+        FKV_CUDA_CHECK(cudaMemsetAsync(const_cast<void*>(workspace), 0, sizeof(word), st));
+    *status = word;
+    return FKV_OK;
 }
 
 int fkv_decode_qk_path(const FkvDecodeShape* sh, const uint8_t* far_k) {
@@ -2041,24 +2076,60 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = 16u << 20;   // 16 MiB per GPU, held until exit
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-constexpr int kMaxDevices = 64;
-void* g_scratch_ptr[kMaxDevices] = {};
+// The array belongs to the CUDA context that loaded this module, so its
+// address is cached per context (the current context, resolved through the
+// runtime's driver entry point), not per device ordinal: a plugin host that
+// drives its own contexts, or a process that resets a device, gets a fresh
+// lookup instead of a stale address.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+struct ScratchEntry {
+    CUcontext ctx;
+    void* ptr;
+};
+std::vector<ScratchEntry> g_scratch;
 std::mutex g_scratch_mu;
 
-// Device address of the scratch array on the current device.  The array's
+CtxGetCurrentFn ctx_get_current_fn() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        cudaDriverEntryPointQueryResult q{};
+        void* f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(f);
+    });
+    return fn;
+}
+
+// Device address of the scratch array in the current context.  The array's
 // host-side name is only a stand-in: the address must come from
-// cudaGetSymbolAddress, queried once per device with that device current.
+// cudaGetSymbolAddress, queried with the device (context) current.
 int noalloc_scratch(void** out) {
     int dev = 0;
     FKV_CUDA_CHECK(cudaGetDevice(&dev));
-    FKV_REQUIRE(dev >= 0 && dev < kMaxDevices, FKV_ERR_UNSUPPORTED, "device %d out of range", dev);
-    std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if (g_scratch_ptr[dev] == nullptr) {
-        void* p = nullptr;
-        FKV_CUDA_CHECK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-        g_scratch_ptr[dev] = p;
+    CtxGetCurrentFn get = ctx_get_current_fn();
+    FKV_REQUIRE(get != nullptr, FKV_ERR_CUDA, "cuCtxGetCurrent unavailable");
+    CUcontext ctx = nullptr;
+    FKV_REQUIRE(get(&ctx) == CUDA_SUCCESS, FKV_ERR_CUDA, "cuCtxGetCurrent failed");
+    if (ctx == nullptr) {
+        // no context yet: a runtime call that needs one makes the device's
+        // primary context current
+        void* probe = nullptr;
+        FKV_CUDA_CHECK(cudaGetSymbolAddress(&probe, g_noalloc_scratch));
+        FKV_REQUIRE(get(&ctx) == CUDA_SUCCESS && ctx != nullptr, FKV_ERR_CUDA,
+                    "no current CUDA context on device %d", dev);
     }
-    *out = g_scratch_ptr[dev];
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    for (const ScratchEntry& e : g_scratch)
+        if (e.ctx == ctx) {
+            *out = e.ptr;
+            return FKV_OK;
+        }
+    void* p = nullptr;
+    FKV_CUDA_CHECK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_scratch.push_back(ScratchEntry{ctx, p});
+    *out = p;
     return FKV_OK;
 }
 
@@ -2074,7 +2145,11 @@ extern "C" int fkv_decode_fp8_noalloc(const FkvDecodeShape* sh, const uint16_t* 
     fkv::clear_error();
     int rc = validate(sh);
     if (rc) return rc;
-    const Plan pl = make_plan(sh, resident_for(sh, false));
+    // the launch may take either q.K path (the tensor-core one falls back to
+    // mma.sync when far_k has no tensor map): accept only shapes whose
+    // scratch fits for both, so the check below is the exact limit
+    const Plan pa = make_plan(sh, resident_for(sh, false)), pb = make_plan(sh, resident_for(sh, false, 0));
+    const Plan& pl = pa.rec_bytes + pa.ticket_bytes >= pb.rec_bytes + pb.ticket_bytes ? pa : pb;
     const size_t need = pl.rec_bytes + pl.ticket_bytes + 256;
     FKV_REQUIRE(need <= kNoAllocScratchBytes, FKV_ERR_INVALID,
                 "fkv_decode_fp8_noalloc: shape needs %zu scratch bytes, above the fixed "
@@ -2089,4 +2164,13 @@ extern "C" int fkv_decode_fp8_noalloc(const FkvDecodeShape* sh, const uint16_t* 
     return fkv_decode_fp8(sh, near_k, near_v, near_valid, far_k, far_v, v_scale, v_zero, q,
                           dec_k, dec_v, out, flags, tokens, scratch, kNoAllocScratchBytes,
                           stream);
+}
+
+extern "C" int fkv_decode_noalloc_status(int32_t* status, void* stream) {
+    fkv::clear_error();
+    FKV_REQUIRE(status != nullptr, FKV_ERR_INVALID, "fkv_decode_noalloc_status: status is NULL");
+    void* scratch = nullptr;
+    const int rc = noalloc_scratch(&scratch);
+    if (rc) return rc;
+    return fkv_decode_status(scratch, status, 0, stream);
 }

@@ -23,7 +23,7 @@ void clear_error() { g_last_error.clear(); }
 
 extern "C" {
 
-int fkv_abi_version(void) { return 1; }
+int fkv_abi_version(void) { return 2; }
 
 const char* fkv_last_error(void) { return fkv::g_last_error.c_str(); }
 

@@ -74,3 +74,47 @@ CONFIGS = {
     "c4": dict(B=1, Hq=32, Hk=8, D=128, S=1 << 20, n_dec=0, near_pct=0.05, n_sinks=4,
                window_size=32, select="recency", v_group=None, compress_method="fp8"),
 }
+
+
+def spike_positions_np(seed: int, B: int, Hk: int, mid_start: int, F: int, frac: float = 0.01):
+    """Seeded positions of the forced spikes: `max(1, int(F * frac))` far
+    positions per (b, kv head) drawn uniformly from [mid_start, mid_start+F)."""
+    n = max(1, int(F * frac))
+    rs = np.random.RandomState(seed + 1)
+    return mid_start + rs.randint(0, F, size=(B, Hk, n))
+
+
+def inject_spikes_np(w: dict, tb: dict, seed: int, frac: float = 0.01):
+    """Turn 1% of the far tokens of each (b, kv head) into spikes (config c3:
+    "keys set to 3 sigma along q"): key = 3 sqrt(D) times the unit mean query
+    of the GQA group, so their scores sit far above the lowest near score.
+    In place on the NumPy workload ``w``; returns the positions."""
+    k, q = w["k"], w["q"]
+    B, Hk, S, D = k.shape
+    G = q.shape[1] // Hk
+    pos = spike_positions_np(seed, B, Hk, tb["mid_start"], tb["far_count"], frac)
+    qm = q.astype(np.float32).reshape(B, Hk, G, D).mean(2)
+    qm /= np.linalg.norm(qm, axis=-1, keepdims=True)
+    val = (3.0 * D ** 0.5 * qm).astype(np.float16)
+    for b in range(B):
+        for h in range(Hk):
+            k[b, h, pos[b, h]] = val[b, h]
+    return pos
+
+
+def inject_spikes_torch(w: dict, tb: dict, seed: int, frac: float = 0.01):
+    """Device version of ``inject_spikes_np`` (same rule, torch generator)."""
+    import torch
+    k, q = w["k"], w["q"]
+    B, Hk, S, D = k.shape
+    G = q.shape[1] // Hk
+    F = tb["far_count"]
+    n = max(1, int(F * frac))
+    g = torch.Generator(device=k.device)
+    g.manual_seed(seed + 1)
+    pos = tb["mid_start"] + torch.randint(0, F, (B, Hk, n), generator=g, device=k.device)
+    qm = q.float().reshape(B, Hk, G, D).mean(2)
+    qm = qm / qm.norm(dim=-1, keepdim=True)
+    val = (3.0 * D ** 0.5 * qm).to(k.dtype)[:, :, None, :].expand(B, Hk, n, D)
+    k.scatter_(2, pos[..., None].expand(B, Hk, n, D), val)
+    return pos

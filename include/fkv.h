@@ -130,7 +130,16 @@ typedef struct FkvDecodeShape {
     int32_t num_splits;    /* split-K chunks per (b,h); 0 = automatic */
     float spike_margin;    /* flag = max_far > min_near + spike_margin */
     float qjl_coef;        /* turbo only: QJL term = qjl_coef/D * gamma * <sign, q S^T> */
+    int32_t wait_limit;    /* iteration limit of the kernel's progress waits; 0 = default
+                              (2^26).  On expiry the kernel records FKV_ERR_TIMEOUT in the
+                              workspace status word (fkv_decode_status), lets its copies
+                              in flight land and exits. */
+    int32_t test_flags;    /* 0 in normal use.  FKV_TEST_STALL: the consumers first wait on
+                              a barrier that nothing completes, so a test can drive the
+                              timeout path (with a small wait_limit) without any fault. */
 } FkvDecodeShape;
+
+#define FKV_TEST_STALL 1
 
 /* Scratch bytes for fkv_decode_fp8 / fkv_decode_turbo / fkv_decode_fp8_partial:
  * split counters (4 bytes per (b, kv head, group of 8 q heads)) at the front
@@ -158,6 +167,14 @@ int fkv_decode_fp8(const FkvDecodeShape* s, const uint16_t* near_k, const uint16
                    const uint16_t* dec_k, const uint16_t* dec_v, uint16_t* out,
                    int32_t* flags, int32_t* tokens, void* workspace, size_t workspace_bytes,
                    void* stream);
+
+/* Kernel status word of the decode calls that used `workspace` (no
+ * counterpart in the reference, whose Metal kernels have no bounded waits):
+ * waits for `stream`, then *status = 0 or FKV_ERR_TIMEOUT (a bounded wait
+ * expired in some launch since the word was last cleared; that launch's
+ * outputs are not valid).  The word is sticky across launches; clear != 0
+ * resets it to 0 (stream-ordered).  Returns FKV_OK or an error of the read. */
+int fkv_decode_status(const void* workspace, int32_t* status, int32_t clear, void* stream);
 
 /* Which q.K path fkv_decode_fp8 / _partial / _noalloc take for this shape
  * and far_k pointer (no counterpart in the reference, whose Metal kernel has
@@ -190,16 +207,24 @@ int fkv_decode_turbo(const FkvDecodeShape* s, const uint16_t* near_k, const uint
  * The split scratch is a fixed 16 MiB device array inside libfkv.so, held by
  * every GPU that loads the library until exit; shapes needing more (see
  * fkv_decode_workspace_bytes) are rejected with FKV_ERR_INVALID.  The first
- * call on a device looks up the array's device address, so make that first
- * call before any stream capture.  All calls share the array (it keeps the
- * last call's contents; each call zeroes the counters it needs): calls that
- * overlap on the GPU race. */
+ * call in a CUDA context looks up the array's address in that context, so
+ * make that first call before any stream capture.  All calls share the array
+ * (it keeps the last call's contents; each call zeroes its status word and
+ * the counters it needs): calls that overlap on the GPU race.  A shape is
+ * accepted exactly when its scratch fits for both q.K paths;
+ * fkv_decode_workspace_bytes(s) <= 16 MiB is sufficient for that but not
+ * necessary. */
 int fkv_decode_fp8_noalloc(const FkvDecodeShape* s, const uint16_t* near_k,
                            const uint16_t* near_v, const int32_t* near_valid,
                            const uint8_t* far_k, const uint8_t* far_v, const uint16_t* v_scale,
                            const uint16_t* v_zero, const uint16_t* q, const uint16_t* dec_k,
                            const uint16_t* dec_v, uint16_t* out, int32_t* flags,
                            int32_t* tokens, void* stream);
+
+/* Status word of the last fkv_decode_fp8_noalloc call in the current
+ * context (read before the next call clears it); same meaning as
+ * fkv_decode_status.  No counterpart in the reference. */
+int fkv_decode_noalloc_status(int32_t* status, void* stream);
 
 /* Sequence-split variant (no reference counterpart; the reference has no
  * multi-device code): same attention over this shard's tiers, but instead of

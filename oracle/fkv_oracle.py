@@ -495,6 +495,79 @@ def decode_attend(layer: dict, q: np.ndarray, dec_k: Optional[np.ndarray] = None
 
 
 # ---------------------------------------------------------------------------
+# The reference's CPU attend in its own precision (timed CPU baseline)
+# ---------------------------------------------------------------------------
+
+_E4M3_LUT = None
+
+
+def _e4m3_lut() -> np.ndarray:
+    global _E4M3_LUT
+    if _E4M3_LUT is None:
+        _E4M3_LUT = e4m3_to_fp16(np.arange(256, dtype=np.uint8))
+    return _E4M3_LUT
+
+
+def reference_attend_f32(layer: dict, q: np.ndarray, dec_k: Optional[np.ndarray] = None,
+                         dec_v: Optional[np.ndarray] = None, threads: int = 1) -> np.ndarray:
+    """``MLXFoveatedLayer.attend`` (mlx_foveated.py:239-278) in the reference's
+    own precision, as the CPU baseline the fused kernel is timed against:
+    far K E4M3 -> fp16 (a 256-entry table lookup, the same bits as
+    ``_e4m3_to_fp16``), far V INT4 -> fp16 in fp16 arithmetic
+    (``_dequant_int4_per_token``: code*scale and +zero, each rounded to fp16),
+    [valid near | decode | far] concatenated, K/V shared by the G query heads
+    of a group (the values ``mx.repeat`` replicates, converted once), then fp32
+    softmax attention with scale 1/sqrt(D) (MLX's CPU SDPA computes fp16
+    inputs in fp32).  No spike tracking or diagnostics: this is the work the
+    reference's CPU path does per decode step.  fp8 far tier, per-token V
+    scales.  The (b, kv head) streams are independent; ``threads`` > 1 runs
+    them on a thread pool (NumPy releases the GIL in these kernels; keep BLAS
+    single-threaded then).  Returns (B, Hq, D) f32.
+    """
+    q = np.asarray(q, dtype=np.float16)
+    B, Hq, D = q.shape
+    Hk = layer["near_k"].shape[1]
+    G = Hq // Hk
+    lut = _e4m3_lut()
+    nv = int(np.max(layer["near_valid"]))
+    scale = np.float32(1.0 / math.sqrt(D))
+    out = np.empty((B, Hq, D), dtype=np.float32)
+    f32, f16 = np.float32, np.float16
+
+    def stream(bh):
+        b, h = divmod(bh, Hk)
+        fk = lut[layer["far_k"][b, h]]
+        pk = layer["far_v"][b, h]
+        codes = np.empty(pk.shape[:-1] + (2 * pk.shape[-1],), dtype=f32)
+        codes[:, 0::2] = pk & 0x0F
+        codes[:, 1::2] = pk >> 4
+        sc = layer["far_v_scale"][b, h][:, None].astype(f32)
+        ze = layer["far_v_zero"][b, h][:, None].astype(f32)
+        # fp16 arithmetic: each operation's exact fp32 result rounded to fp16
+        fv = ((codes * sc).astype(f16).astype(f32) + ze).astype(f16)
+        ks = [layer["near_k"][b, h, :nv]]
+        vs = [layer["near_v"][b, h, :nv]]
+        if dec_k is not None and dec_k.shape[2] > 0:
+            ks.append(dec_k[b, h])
+            vs.append(dec_v[b, h])
+        k32 = np.concatenate(ks + [fk]).astype(f32)
+        v32 = np.concatenate(vs + [fv]).astype(f32)
+        qg = q[b, h * G:(h + 1) * G].astype(f32) * scale
+        sc_ = qg @ k32.T
+        p = np.exp(sc_ - sc_.max(axis=1, keepdims=True))
+        out[b, h * G:(h + 1) * G] = (p @ v32) / p.sum(axis=1, keepdims=True)
+
+    if threads > 1:
+        from concurrent.futures import ThreadPoolExecutor
+        with ThreadPoolExecutor(threads) as ex:
+            list(ex.map(stream, range(B * Hk)))
+    else:
+        for bh in range(B * Hk):
+            stream(bh)
+    return out
+
+
+# ---------------------------------------------------------------------------
 # Split-sequence combine (multi-GPU; no reference counterpart)
 # ---------------------------------------------------------------------------
 

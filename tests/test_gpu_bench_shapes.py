@@ -1,0 +1,171 @@
+"""GPU parity at the benchmarked shapes (configs c1, c2, c3 and c4).
+
+Each benchmark line is only as good as the parity behind it, so the shapes the
+bench measures are decoded here too and compared with the CPU oracle:
+
+* c3 slice: B=2 of the 64 sequences, Hq32/Hk8, D128, S=32K, window 32, 10%
+  near, with the benchmark's 1% injected spikes (keys 3 sigma along the
+  group's mean query) at margin 0.5.  Every flag fires and every token is the
+  earliest of the identical spike keys, so the tie-break is exercised too.
+  The compressed tiers are checked bit for bit against the oracle first.
+* c1 at S = 4K and 16K (G = 1, 32 KV heads; 9-13 splits per stream).
+* c2: TurboQuant at S = 16K, Hq28/Hk4, with the planner's own split count
+  (beyond the direct-load merge, i.e. the bulk-copy merge path).
+* c4 long split: a 256K-token sequence, Hq32/Hk8, 5% near, split into 8
+  equal-cost shards on one GPU (partial kernel per shard + combine), against
+  the oracle's attention over the unsplit tiers.
+
+Tolerances are the parity bar of the other decode tests (tests/helpers.py):
+output max-abs 2e-3 and cosine 0.9999; flags and tokens identical.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import fkv_oracle as O
+from foveated_kv_b200 import TierConfig, compress_layer
+from foveated_kv_b200.synthetic import numpy_workload, inject_spikes_np, CONFIGS
+from foveated_kv_b200.turbo_constants import host_constants
+from tests.helpers import np_, bits, layer_to_oracle, assert_output_close, assert_spikes_match
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg(name, **over):
+    c = dict(CONFIGS[name])
+    c.update(over)
+    return c
+
+
+def _tier_cfg(c, margin=0.5):
+    return TierConfig(near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
+                      v_group=c["v_group"], compress_method=c["compress_method"],
+                      select=c["select"], spike_margin=margin)
+
+
+def _oracle_cfg(c):
+    return dict(near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
+                v_group=c["v_group"], compress_method=c["compress_method"], select=c["select"])
+
+
+@pytest.fixture(params=["tcgen05", "mma"])
+def qk_path(request, monkeypatch):
+    monkeypatch.setenv("FKV_QK_PATH", request.param)
+    return request.param
+
+
+def _decode_and_check(lay, w, margin, name, tc=None):
+    t_q = torch.from_numpy(w["q"]).cuda()
+    out, fl, tk = lay.attend_fused_with_spikes(t_q)
+    torch.cuda.synchronize()
+    rout, rfl, rtk, diag = O.decode_attend(layer_to_oracle(lay, tc), w["q"], None, None, margin)
+    err, cos = assert_output_close(np_(out).astype(np.float64)[:, :, 0], rout, name)
+    ties = assert_spikes_match(np_(fl), np_(tk), rfl, rtk, diag, margin, name)
+    assert ties == 0, f"{name}: {ties} spike decisions within the tie band"
+    return err, cos, np_(fl), np_(tk)
+
+
+# ---- c3 slice with injected spikes ------------------------------------------------
+
+@pytest.fixture(scope="module")
+def c3_slice():
+    c = _cfg("c3", B=2)
+    w = numpy_workload(71, c["B"], c["Hk"], c["Hq"], c["S"], c["D"], 0)
+    tb = O.tier_boundaries(c["S"], near_pct=c["near_pct"], n_sinks=c["n_sinks"],
+                           window_size=c["window_size"])
+    pos = inject_spikes_np(w, tb, 71)
+    ref = O.compress_layer(w["k"], w["v"], _oracle_cfg(c))
+    t = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
+    lay = compress_layer(t["k"], t["v"], _tier_cfg(c))
+    torch.cuda.synchronize()
+    del t
+    return c, w, pos, ref, lay
+
+
+def test_c3_slice_tiers_bit_exact(c3_slice):
+    c, w, pos, ref, lay = c3_slice
+    for f in ["near_k", "near_v", "near_idx", "near_valid", "far_idx", "far_k", "far_v",
+              "far_v_scale", "far_v_zero", "archive_k", "archive_v"]:
+        a, b = bits(np_(getattr(lay, f))), bits(ref[f])
+        assert np.array_equal(a, b), f"c3 slice: {f} differs in {int((a != b).sum())} places"
+
+
+def test_c3_slice_decode_with_spikes(c3_slice, qk_path):
+    c, w, pos, ref, lay = c3_slice
+    err, cos, fl, tk = _decode_and_check(lay, w, 0.5, f"c3 slice ({qk_path})")
+    G = c["Hq"] // c["Hk"]
+    assert fl.all(), "every head of the c3 slice holds forced spikes"
+    # the spikes are identical keys: the token is the earliest spike position
+    far0 = O.tier_boundaries(c["S"], near_pct=c["near_pct"], n_sinks=c["n_sinks"],
+                             window_size=c["window_size"])["mid_start"]
+    want = (pos.min(axis=2) - far0).repeat(G, axis=1)
+    assert np.array_equal(tk, want)
+    print(f"c3 slice {qk_path}: max-abs {err:.2e} cos {cos:.7f}")
+
+
+# ---- c1 at 4K and 16K ----------------------------------------------------------------
+
+@pytest.mark.parametrize("name", ["c1_4k", "c1_16k"])
+def test_c1_decode(name, qk_path):
+    c = _cfg(name)
+    w = numpy_workload(72, c["B"], c["Hk"], c["Hq"], c["S"], c["D"], 0)
+    t = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
+    lay = compress_layer(t["k"], t["v"], _tier_cfg(c))
+    err, cos, _, _ = _decode_and_check(lay, w, 0.5, f"{name} ({qk_path})")
+    print(f"{name} {qk_path}: max-abs {err:.2e} cos {cos:.7f}")
+
+
+# ---- c2: TurboQuant at 16K ------------------------------------------------------------
+
+def test_c2_turbo_decode_16k():
+    c = _cfg("c2")
+    w = numpy_workload(73, c["B"], c["Hk"], c["Hq"], c["S"], c["D"], 0)
+    t = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
+    lay = compress_layer(t["k"], t["v"], _tier_cfg(c))
+    pi, s, cen, bnd = host_constants(c["D"])
+    tc = {"Pi": pi, "S": s, "centroids": cen, "boundaries": bnd}
+    err, cos, _, _ = _decode_and_check(lay, w, 0.5, "c2 turbo 16K", tc)
+    print(f"c2: max-abs {err:.2e} cos {cos:.7f}")
+
+
+# ---- c4: long sequence split into 8 shards on one GPU ------------------------------
+
+@pytest.fixture(scope="module")
+def c4_long():
+    c = _cfg("c4", S=1 << 18)
+    B, Hq, Hk, D, S = c["B"], c["Hq"], c["Hk"], c["D"], c["S"]
+    w = numpy_workload(74, B, Hk, Hq, S, D, 0)
+    tb = O.tier_boundaries(S, near_pct=c["near_pct"], n_sinks=c["n_sinks"],
+                           window_size=c["window_size"])
+    inject_spikes_np(w, tb, 74, frac=0.001)
+    t = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
+    full = compress_layer(t["k"], t["v"], _tier_cfg(c), keep_archive=False)
+    torch.cuda.synchronize()
+    ref = O.decode_attend(layer_to_oracle(full), w["q"], None, None, 0.5)
+    del full
+    return c, t, ref
+
+
+def test_c4_long_split_eight_shards(c4_long, qk_path):
+    from foveated_kv_b200.seqsplit import shard_bounds_balanced, compress_shard, decode_partial, combine
+    c, t, (rout, rfl, rtk, diag) = c4_long
+    B, Hq, D, S = c["B"], c["Hq"], c["D"], c["S"]
+    cfg = _tier_cfg(c)
+    P = 8
+    parts, args = [], []
+    for r in range(P):
+        lo, hi = shard_bounds_balanced(S, r, P, cfg)
+        lay, off = compress_shard(t["k"][:, :, lo:hi], t["v"][:, :, lo:hi], S, lo, cfg)
+        pa, ar = decode_partial(lay, t["q"], off)
+        parts.append(pa.clone())
+        args.append(ar.clone())
+        del lay
+    out, fl, tk = combine(torch.stack(parts), torch.stack(args), 0.5)
+    torch.cuda.synchronize()
+    err, cos = assert_output_close(np_(out).astype(np.float64).reshape(B, Hq, D), rout, "c4 split")
+    ties = assert_spikes_match(np_(fl).reshape(B, Hq), np_(tk).reshape(B, Hq), rfl, rtk, diag,
+                               0.5, "c4 split")
+    assert ties == 0
+    assert np_(fl).all()
+    print(f"c4 256K split x{P} {qk_path}: max-abs {err:.2e} cos {cos:.7f}")

@@ -30,7 +30,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_error_string():
     lib = _native.load()
-    assert lib.fkv_abi_version() == 1
+    assert lib.fkv_abi_version() == 2
     assert isinstance(lib.fkv_last_error(), bytes)
 
 

@@ -201,3 +201,25 @@ def test_product_turbo_constants_match_reference(golden, d):
     t = golden("turbo_constants.npz")
     for k, v in zip(("Pi", "S", "centroids", "boundaries"), host_constants(d)):
         assert np.array_equal(v, t[f"{k}_{d}"]), k
+
+
+def test_reference_attend_f32_matches_reference_and_oracle(golden):
+    """The timed CPU baseline (the reference's attend in its own precision)
+    agrees with the reference-generated c0 output and with the fp64 oracle,
+    single-threaded and on a thread pool alike."""
+    A = golden("attend_c0.npz")
+    c = CONFIGS["c0"]
+    w = numpy_workload(100, c["B"], c["Hk"], c["Hq"], c["S"], c["D"], c["n_dec"])
+    lay = O.compress_layer(w["k"], w["v"], dict(window_size=64))
+    o1 = O.reference_attend_f32(lay, w["q"], threads=1)
+    o4 = O.reference_attend_f32(lay, w["q"], threads=4)
+    assert np.array_equal(o1, o4)
+    assert np.abs(o1 - A["out"].reshape(o1.shape).astype(np.float32)).max() < 2e-3
+    ref, _, _, _ = O.decode_attend(lay, w["q"])
+    assert np.abs(o1 - ref).max() < 1e-5
+    # with a decode buffer
+    wd = numpy_workload(101, 2, 2, 8, 700, 128, 5)
+    lay = O.compress_layer(wd["k"], wd["v"], dict(window_size=16))
+    o = O.reference_attend_f32(lay, wd["q"], wd["dec_k"], wd["dec_v"], threads=2)
+    ref, _, _, _ = O.decode_attend(lay, wd["q"], wd["dec_k"], wd["dec_v"])
+    assert np.abs(o - ref).max() < 1e-5

@@ -60,11 +60,18 @@ def _run(lay, q, noalloc):
 def test_noalloc_matches_workspace_entry_twice(shape):
     lay, q = _layer(31, *shape)
     ref = _run(lay, q, noalloc=False)
+    lib = _native.load()
     for _ in range(2):   # second call reuses the scratch left by the first
         got = _run(lay, q, noalloc=True)
         assert np.abs(got[0] - ref[0]).max() <= OUT_MAX_ABS
         assert np.array_equal(got[1], ref[1])
         assert np.array_equal(got[2], ref[2])
+        # the kernel status word of the call (kept in the fixed scratch) is clean
+        st = C.c_int32(123)
+        _native.check(lib.fkv_decode_noalloc_status(C.byref(st),
+                                                    torch.cuda.current_stream().cuda_stream),
+                      "fkv_decode_noalloc_status")
+        assert st.value == 0
 
 
 def test_noalloc_rejects_oversized_shape():
