@@ -315,18 +315,23 @@ def sdpa_fp16_baseline(c, device, steps, warmup, layers_bytes=4e9, flashinfer=Fa
 
 
 def qk_path_name(lay, Hq: int) -> str:
-    """The q.K path the fused decode takes for this layer (reported in config)."""
+    """The q.K path and launch shape the fused decode takes for this layer
+    (reported in config)."""
     import ctypes as C
-    import torch
     from foveated_kv_b200 import _native
-    if lay.far_k is None or lay.n_far == 0 or lay.far_k.dtype != torch.uint8:
-        return "mma.sync"
-    if lay.far_k.shape[-1] != lay.near_k.shape[-1]:
-        return "mma.sync (TurboQuant codes)"
     lib = _native.load()
+    turbo = lay.compress_method == "turbo"
     sh = lay._fill_shape(Hq, lay.spike_margin)
-    nh = lib.fkv_decode_qk_path(C.byref(sh), lay.far_k.data_ptr())
-    return f"tcgen05.mma f8f6f4 ({nh} q heads/CTA)" if nh > 0 else "mma.sync"
+    far = lay.far_k.data_ptr() if (not turbo and lay.far_k is not None and lay.far_k.numel()) else None
+    out = (C.c_int32 * 4)()
+    _native.check(lib.fkv_decode_plan(C.byref(sh), far, int(turbo), out), "fkv_decode_plan")
+    nh, splits, csize, groups = list(out)
+    path = (f"tcgen05.mma f8f6f4 ({nh} q heads/CTA)" if nh > 0 else
+            "mma.sync (TurboQuant codes)" if turbo else "mma.sync")
+    launch = (f"{splits} CTAs/stream in {groups} cluster(s) of {csize} (dynamic stages, DSMEM merge)"
+              if csize >= 2 else f"{splits} CTAs/stream (workspace merge)")
+    return f"{path}; {launch}"
+
 
 def main_seqsplit(args, rank, world, device):
     """c4: one 1M-token sequence split evenly over the ranks; per step each

@@ -70,6 +70,7 @@ SIGNATURES = {
     "fkv_decode_workspace_bytes": (SZ, [C.POINTER(DecodeShape)]),
     "fkv_decode_qk_path": (C.c_int, [C.POINTER(DecodeShape), P]),
     "fkv_decode_status": (C.c_int, [P, C.POINTER(I32), I32, P]),
+    "fkv_decode_plan": (C.c_int, [C.POINTER(DecodeShape), P, I32, P]),
     "fkv_decode_noalloc_status": (C.c_int, [C.POINTER(I32), P]),
     "fkv_decode_fp8": (C.c_int, [C.POINTER(DecodeShape), P, P, P, P, P, P, P, P, P, P, P, P,
                                  P, P, SZ, P]),

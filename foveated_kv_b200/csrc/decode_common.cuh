@@ -370,3 +370,45 @@ __device__ __forceinline__ void tmem_wait_ld() {
 }
 
 }  // namespace fkvdev
+
+// ---------------------------------------------------------------------------
+// Thread-block cluster primitives: cluster barrier (all threads of every CTA
+// of the cluster, whole warps), distributed shared memory addressing and
+// loads / atomics into a peer CTA's shared memory.
+// ---------------------------------------------------------------------------
+namespace fkvdev {
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t peer_smem(const void* local, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(out) : "r"(smem_u32(local)), "r"(rank));
+    return out;
+}
+__device__ __forceinline__ float ld_peer_f32(uint32_t addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_peer_s32(uint32_t addr) {
+    int v;
+    asm volatile("ld.shared::cluster.s32 %0, [%1];\n" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t atom_add_peer(uint32_t addr, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.shared::cluster.add.u32 %0, [%1], %2;\n" : "=r"(old) : "r"(addr), "r"(v) : "memory");
+    return old;
+}
+
+}  // namespace fkvdev

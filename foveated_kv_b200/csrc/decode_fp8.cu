@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -66,6 +67,7 @@ struct DecodeParams {
     const float* turbo_s;
     float qjl_coef;
     int B, Hq, Hk, G, HG, Np, F, n_dec, dec_stride, splits;
+    int csize, groups;    // cluster mode: CTAs per cluster, clusters per (stream, head group)
     int near_w, far_w;    // cost units of an fp16 near / decode token and of a far token
     float margin, qscale;
 };
@@ -225,7 +227,15 @@ struct Ring {
     static constexpr int BAROFF = TSUM + (VG == kTurbo ? 64 : 0);        // mbarriers
     static constexpr int MERGEBAR = BAROFF + 2 * kStages * 8;          // 2 split-merge barriers
     static constexpr int STALLBAR = MERGEBAR + 2 * 8;                  // never completed (test hook)
-    static constexpr int BYTES = STALLBAR + 8;   // (+1024 at launch: base alignment slack)
+    // cluster mode: per-slot stage headers, the cluster's stage counter (used
+    // in rank 0), stages issued, producer done
+    static constexpr int CTRL = STALLBAR + 8;
+    static constexpr int HDR = CTRL, COUNTER = CTRL + 4 * kStages, ISSUED = COUNTER + 4,
+                         PDONE = ISSUED + 4;
+    // turbo in cluster mode: q Pi^T | q S^T of the CTA's 8 q heads (f32)
+    static constexpr int QPJ = (PDONE + 4 + 15) & ~15;
+    static constexpr int BYTES = QPJ + (VG == kTurbo ? kHeadsPerTile * 2 * D * 4 : 0);
+    // (+1024 at launch: base alignment slack)
 };
 
 // Extra shared memory of the tensor-core far path (placed after the ring's
@@ -423,14 +433,19 @@ __device__ __forceinline__ void far_tail(const float (&sv)[4 * NT],
     }
     // spike tracker: the lane's values are in token order, so the earliest
     // index of a new strict maximum is the first j holding it (rare branch)
-    if (lm > st.mf) {
+    // (stages may arrive out of token order in cluster mode: an equal
+    // maximum replaces the tracked one when its index is lower)
+    if (lm >= st.mf && lm != -INFINITY) {
         int jj = 0;
 #pragma unroll
         for (int j = 4 * NT - 1; j >= 0; --j)
             if (s[j] == lm) jj = j;
-        st.mf = lm;
         const int ut = (NT > 1 && jj >= 4) ? u0[NT - 1] : u0[0];
-        st.af = gbase + ut + ((jj & 3) >> 1) * 8 + 2 * c + (jj & 1);
+        const int idx = gbase + ut + ((jj & 3) >> 1) * 8 + 2 * c + (jj & 1);
+        if (lm > st.mf || idx < st.af) {
+            st.mf = lm;
+            st.af = idx;
+        }
     }
     st.softmax_step(s, pr, lm, lane);
 #pragma unroll
@@ -664,14 +679,19 @@ __global__ void __launch_bounds__(kQpThreads)
 }
 
 // hi/lo fragments of q Pi^T and q S^T in the turbo permutation + per-head sums
+// (qsh != nullptr: the projections of the CTA's 8 heads are in shared memory,
+// head r at qsh + r * 2D, as the cluster mode computes them)
 template <int D>
 __device__ __forceinline__ void build_turbo_frags(const DecodeParams& p, int s, int hg, int lane,
                                                   uint4* __restrict__ qr, uint4* __restrict__ qk,
-                                                  float* __restrict__ sums) {
+                                                  float* __restrict__ sums,
+                                                  const float* qsh = nullptr) {
     const int r = lane >> 2, c = lane & 3;
     const int b = s / p.Hk, h = s % p.Hk;
     const int g = hg * kHeadsPerTile + r;
-    const float* src = g < p.G ? p.qproj + ((int64_t)b * p.Hq + (int64_t)h * p.G + g) * 2 * D : nullptr;
+    const float* src = g >= p.G ? nullptr
+                       : qsh != nullptr ? qsh + r * 2 * D
+                                        : p.qproj + ((int64_t)b * p.Hq + (int64_t)h * p.G + g) * 2 * D;
     float sr = 0.f, sk = 0.f;
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
@@ -681,7 +701,8 @@ __device__ __forceinline__ void build_turbo_frags(const DecodeParams& p, int s, 
             __half hi[4], lo[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float v = src ? __ldg(src + which * D + 4 * (4 * j + c) + e) : 0.f;
+                const int o = which * D + 4 * (4 * j + c) + e;
+                const float v = src == nullptr ? 0.f : qsh != nullptr ? src[o] : __ldg(src + o);
                 if (which) sk += v; else sr += v;
                 hi[e] = __float2half_rn(v);
                 lo[e] = __float2half_rn(v - __half2float(hi[e]));
@@ -788,7 +809,7 @@ __device__ __forceinline__ void turbo_tile(const uint8_t* __restrict__ sgn,
         const float qjl = cf[4] * f.y * fmaf(2.f, sgn, -sum_k);
         const float v = fmaf(f.x, mse, qjl) * cf[5];
         s[j] = u < cnt ? v : -INFINITY;
-        if (u < cnt && v > st.mf) {
+        if (u < cnt && (v > st.mf || (v == st.mf && gbase + u < st.af))) {
             st.mf = v;
             st.af = gbase + u;
         }
@@ -823,6 +844,53 @@ __device__ __forceinline__ void turbo_tile(const uint8_t* __restrict__ sgn,
             }
         }
         mma16816(st.o[i], a, pb0, pb1);
+    }
+}
+
+// Cluster mode, TurboQuant: the q Pi^T | q S^T projections of the cluster's
+// 8 q heads are computed in slices, rank r taking output columns
+// [r * cw, (r + 1) * cw) of the 2D, then gathered from the peers' shared
+// memory.  Each output is the same fp32 dot product, in the same order, as
+// turbo_qproj_kernel computes.
+template <int D>
+__device__ __forceinline__ void turbo_qproj_slice(const DecodeParams& p, int s, int hg, int crank,
+                                                  float* __restrict__ qpj) {
+    const int C = p.csize;
+    const int cw = (2 * D + C - 1) / C, c0 = crank * cw;
+    const int nc = max(0, min(2 * D, c0 + cw) - c0);
+    const int b = s / p.Hk, h = s % p.Hk;
+    for (int idx = threadIdx.x; idx < kHeadsPerTile * nc; idx += kConsumerThreads) {
+        const int hh = idx / nc, col = c0 + idx % nc;
+        const int g = hg * kHeadsPerTile + hh;
+        float acc = 0.f;
+        if (g < p.G) {
+            const uint16_t* qrow = p.q + ((int64_t)b * p.Hq + (int64_t)h * p.G + g) * D;
+            const float* mrow = col < D ? p.turbo_pi + (int64_t)col * D : p.turbo_s + (int64_t)(col - D) * D;
+#pragma unroll 4
+            for (int i = 0; i < D; i += 8) {
+                const uint4 qw = __ldg(reinterpret_cast<const uint4*>(qrow + i));
+                const float4 m0 = __ldg(reinterpret_cast<const float4*>(mrow + i));
+                const float4 m1 = __ldg(reinterpret_cast<const float4*>(mrow + i + 4));
+                const float2 a = __half22float2(u32_as_h2(qw.x)), bq = __half22float2(u32_as_h2(qw.y));
+                const float2 cq = __half22float2(u32_as_h2(qw.z)), dq = __half22float2(u32_as_h2(qw.w));
+                acc = fmaf(a.x, m0.x, acc); acc = fmaf(a.y, m0.y, acc);
+                acc = fmaf(bq.x, m0.z, acc); acc = fmaf(bq.y, m0.w, acc);
+                acc = fmaf(cq.x, m1.x, acc); acc = fmaf(cq.y, m1.y, acc);
+                acc = fmaf(dq.x, m1.z, acc); acc = fmaf(dq.y, m1.w, acc);
+            }
+        }
+        qpj[hh * 2 * D + col] = acc;
+    }
+}
+
+template <int D>
+__device__ __forceinline__ void turbo_qproj_gather(const DecodeParams& p, int crank,
+                                                   float* __restrict__ qpj) {
+    const int C = p.csize;
+    const int cw = (2 * D + C - 1) / C;
+    for (int idx = threadIdx.x; idx < kHeadsPerTile * 2 * D; idx += kConsumerThreads) {
+        const int owner = (idx % (2 * D)) / cw;
+        if (owner != crank) qpj[idx] = ld_peer_f32(peer_smem(qpj + idx, (uint32_t)owner));
     }
 }
 
@@ -1051,10 +1119,107 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, const float*
     merge_emit<D>(p, acc, s, hg, scratch);
 }
 
+// Cluster mode: merge the csize CTA records of one cluster (each in its CTA's
+// shared memory at `crec`) through distributed shared memory.  The 8 x D
+// outputs are spread over the cluster's consumer threads; every thread loads
+// the (m, l, o) of its element from each rank in one round, then emits the
+// output (or the sequence-split record, or, with several groups per stream,
+// the cluster's record in the workspace).  Rank 0 merges the spike trackers.
+constexpr int kMaxCluster = 16;
+
+template <int D>
+__device__ __forceinline__ void cluster_merge(const DecodeParams& p, int s, int hg, int grp,
+                                              int crank, const float* crec) {
+    using R = RecLayout<D>;
+    const int C = p.csize;
+    const int b = s / p.Hk, h = s % p.Hk;
+    uint32_t base[kMaxCluster];
+#pragma unroll
+    for (int k = 0; k < kMaxCluster; ++k) base[k] = k < C ? peer_smem(crec, (uint32_t)k) : 0u;
+    float* grec = p.groups > 1 ? p.ws + (((int64_t)s * p.HG + hg) * p.groups + grp) * R::SIZE : nullptr;
+    for (int e = crank * kConsumerThreads + (int)threadIdx.x; e < kHeadsPerTile * D;
+         e += C * kConsumerThreads) {
+        const int head = e / D, d = e % D;
+        float mv[kMaxCluster], lv[kMaxCluster], ov[kMaxCluster];
+#pragma unroll
+        for (int k = 0; k < kMaxCluster; ++k) {
+            if (k < C) {
+                mv[k] = ld_peer_f32(base[k] + 4u * (R::M + head));
+                lv[k] = ld_peer_f32(base[k] + 4u * (R::L + head));
+                ov[k] = ld_peer_f32(base[k] + 4u * (R::O + e));
+            }
+        }
+        float M = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < kMaxCluster; ++k)
+            if (k < C) M = fmaxf(M, mv[k]);
+        float L = 0.f, acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < kMaxCluster; ++k) {
+            if (k < C) {
+                const float wgt = mv[k] == -INFINITY ? 0.f : exp2f((mv[k] - M) * kLog2e);
+                L = fmaf(wgt, lv[k], L);
+                acc = fmaf(wgt, ov[k], acc);
+            }
+        }
+        const int g = hg * kHeadsPerTile + head;
+        if (grec != nullptr) {
+            grec[R::O + e] = acc;
+            if (d == 0) {
+                grec[R::M + head] = M;
+                grec[R::L + head] = L;
+            }
+        } else if (g < p.G) {
+            const int64_t bh = (int64_t)b * p.Hq + (int64_t)h * p.G + g;
+            if (p.part != nullptr) {
+                p.part[bh * (D + 4) + 4 + d] = acc;
+                if (d == 0) {
+                    p.part[bh * (D + 4)] = M;
+                    p.part[bh * (D + 4) + 1] = L;
+                }
+            } else {
+                p.out[bh * D + d] = __half_as_ushort(__float2half_rn(L > 0.f ? acc / L : 0.f));
+            }
+        }
+    }
+    if (crank == 0 && threadIdx.x < kHeadsPerTile) {
+        const int head = threadIdx.x;
+        float mn = INFINITY, mf = -INFINITY;
+        int af = -1;
+        for (int k = 0; k < C; ++k) {
+            const uint32_t bk = peer_smem(crec, (uint32_t)k);
+            mn = fminf(mn, ld_peer_f32(bk + 4u * (R::MN + head)));
+            argmax_merge(mf, af, ld_peer_f32(bk + 4u * (R::MF + head)), ld_peer_s32(bk + 4u * (R::AF + head)));
+        }
+        const int g = hg * kHeadsPerTile + head;
+        if (grec != nullptr) {
+            grec[R::MN + head] = mn;
+            grec[R::MF + head] = mf;
+            grec[R::AF + head] = __int_as_float(af);
+        } else if (g < p.G) {
+            const int64_t bh = (int64_t)b * p.Hq + (int64_t)h * p.G + g;
+            if (p.part != nullptr) {
+                p.part[bh * (D + 4) + 2] = mn;
+                p.part[bh * (D + 4) + 3] = mf;
+                p.part_arg[bh] = af >= 0 ? af + p.far_offset : -1;
+            } else {
+                p.flags[bh] = (mf > mn + p.margin) ? 1 : 0;
+                p.tokens[bh] = af;
+            }
+        }
+    }
+}
+
 // NH = 0: far-tier q.K on mma.sync after converting the codes; NH = 4 or 8:
 // far-tier q.K on tcgen05 (NH q heads per CTA, D = 128, E4M3 K; maps.far_k
 // is used only then).
-template <int D, int VG, int NH = 0>
+// CL: cluster mode.  The CTAs of one cluster share the stage range of one
+// (stream, head group, group of the stream's cost ranges): the first kStages
+// stages are dealt round robin, the rest claimed one at a time through a
+// counter in the shared memory of cluster rank 0, so CTAs that run faster
+// take more stages; the CTA records are then merged through distributed
+// shared memory instead of global records and a ticket.
+template <int D, int VG, int NH = 0, bool CL = false>
 __global__ void __maxnreg__(NH > 0 ? 128 : 136)
     decode_fp8_kernel(const DecodeParams p, const __grid_constant__ TMaps maps) {
     using R = RecLayout<D>;
@@ -1062,6 +1227,7 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
     using UL = UmLayout<D, VG>;
     constexpr bool UM = NH > 0;
     static_assert(!UM || (D == 128 && VG != kTurbo), "tensor-core far path: fp8 K, D = 128");
+    static_assert(!(UM && CL), "cluster mode runs on the mma.sync far path");
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // 1024-byte aligned base: the swizzled TMA boxes and UMMA operands
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1069,8 +1235,16 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
     uint4* qs = reinterpret_cast<uint4*>(smem + RG::QOFF);
     uint64_t* empty = full + kStages;
     __shared__ int sh_last;
-    const int split = blockIdx.x, hg = blockIdx.y, s = blockIdx.z;
+    const int hg = blockIdx.y, s = blockIdx.z;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    // cluster mode: this CTA's rank in its cluster and the cluster's group;
+    // the group plays the role of the split in the cost-range cut below
+    const int crank = CL ? (int)cluster_rank() : 0;
+    const int split = CL ? (int)blockIdx.x / p.csize : (int)blockIdx.x;
+    const int nsplit = CL ? p.groups : p.splits;
+    int* hdr = reinterpret_cast<int*>(smem + RG::HDR);
+    volatile int* issued_c = reinterpret_cast<volatile int*>(smem + RG::ISSUED);
+    volatile int* pdone = reinterpret_cast<volatile int*>(smem + RG::PDONE);
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kStages; ++i) {
@@ -1080,6 +1254,12 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
         mbar_init(reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR), 1);
         mbar_init(reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR) + 1, 1);
         mbar_init(reinterpret_cast<uint64_t*>(smem + RG::STALLBAR), 1);
+        if constexpr (CL) {
+            // rank 0's counter: the first kStages * csize stages are dealt round robin
+            *reinterpret_cast<uint32_t*>(smem + RG::COUNTER) = (uint32_t)(kStages * p.csize);
+            *issued_c = 0;
+            *pdone = 0;
+        }
         if constexpr (UM) {
             for (int i = 0; i < kStages; ++i) mbar_init(reinterpret_cast<uint64_t*>(smem + UL::MMAB) + i, 1);
             mbar_init(reinterpret_cast<uint64_t*>(smem + UL::QREADY), 3);   // TMEM + 2 piece warps
@@ -1100,7 +1280,7 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
         if (cu <= cost_nf) return nv + (int)((cu - cost_near) / fw);
         return nv + p.F + (int)((cu - cost_nf) / nw);
     };
-    const int64_t chunk = (total_cost + p.splits - 1) / p.splits;
+    const int64_t chunk = (total_cost + nsplit - 1) / nsplit;
     const int t0 = to_tok(min((int64_t)split * chunk, total_cost));
     const int t1 = to_tok(min((int64_t)(split + 1) * chunk, total_cost));
     Segs sg;
@@ -1116,12 +1296,13 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
 
     if (w == kConsumerWarps) {
         // ---------------- producer warp: one elected lane issues bulk copies
-        if (lane == 0) {
+        [[maybe_unused]] int j = 0;          // cluster mode: stages put into this CTA's ring
+        [[maybe_unused]] bool done = false;  // cluster mode: the sentinel header is out
+        {
             const uint8_t* fk = p.far_k + (int64_t)s * p.F * D;
             const uint8_t* fv = p.far_v + (int64_t)s * p.F * (D / 2);
             // copies of stage k into slot k % kStages, completing on full[slot]
-            auto issue = [&](int k) {
-                const int slot = k % kStages;
+            auto issue = [&](int k, int slot) {
                 int seg, start, cnt;
                 stage_at<D>(sg, k, seg, start, cnt);
                 uint8_t* dst = smem + slot * RG::SLOT;
@@ -1183,14 +1364,32 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
                 }
                 mbar_arrive_expect_tx(full + slot, tx);
             };
-            if constexpr (!UM) {
+            if (lane != 0) {
+                // only the elected lane issues
+            } else if constexpr (CL) {
+                // first kStages stages dealt round robin (no wait: the slots
+                // are free), then one claim per freed slot from rank 0's
+                // counter (below); a claim past the end becomes a sentinel
+                for (; j < kStages; ++j) {
+                    const int k = crank + j * p.csize;
+                    hdr[j] = k < nstage ? k : -1;
+                    if (k >= nstage) {
+                        mbar_arrive(full + j);
+                        ++j;
+                        done = true;
+                        break;
+                    }
+                    issue(k, j);
+                }
+                *issued_c = j;
+            } else if constexpr (!UM) {
                 for (int k = 0; k < nstage; ++k) {
                     if (k >= kStages &&
                         !mbar_wait(empty + k % kStages, ((k / kStages) - 1) & 1, p.wait_limit)) {
                         atomicExch(p.status, FKV_ERR_TIMEOUT);
                         break;
                     }
-                    issue(k);
+                    issue(k, k % kStages);
                 }
             } else {
                 // Two event streams polled without blocking: refill a slot as
@@ -1235,7 +1434,7 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
                     }
                     if (kc < nstage &&
                         (kc < kStages || mbar_test(empty + kc % kStages, ((kc / kStages) - 1) & 1))) {
-                        issue(kc);
+                        issue(kc, kc % kStages);
                         ++kc;
                         prog = true;
                     }
@@ -1255,6 +1454,38 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
                 if (any_mma) umma_commit(drain);
                 else mbar_arrive(drain);
             }
+            if constexpr (CL) {
+                __syncwarp();
+                cluster_arrive();   // start barrier: rank 0's counter is set, every CTA runs
+                cluster_wait();
+                if (lane == 0) {
+                    const uint32_t ctr = peer_smem(smem + RG::COUNTER, 0);
+                    while (!done) {
+                        const int slot = j % kStages;
+                        if (!mbar_wait(empty + slot, ((j / kStages) - 1) & 1, p.wait_limit)) {
+                            atomicExch(p.status, FKV_ERR_TIMEOUT);
+                            break;
+                        }
+                        const int k = (int)atom_add_peer(ctr, 1u);
+                        hdr[slot] = k < nstage ? k : -1;
+                        if (k < nstage) {
+                            issue(k, slot);
+                        } else {
+                            mbar_arrive(full + slot);
+                            done = true;
+                        }
+                        ++j;
+                        *issued_c = j;
+                    }
+                    __threadfence_block();
+                    *pdone = 1;
+                }
+                __syncwarp();
+                cluster_arrive();   // end barrier 1: the CTA records are in shared memory
+                cluster_wait();
+                cluster_arrive();   // end barrier 2: the merge has read them
+                cluster_wait();
+            }
         }
         return;
     }
@@ -1268,11 +1499,23 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
     // at the end) while warps 2 and 3 build the q-piece B operand
     if (w == 0) {
         build_q_frags<D>(p, s, hg, lane, qs);
-        if constexpr (VG == kTurbo) {
+        if constexpr (VG == kTurbo && !CL) {
             // q Pi^T / q S^T come from turbo_qproj_kernel, which may still be
             // running (programmatic dependent launch): wait for it here only
             asm volatile("griddepcontrol.wait;\n" ::: "memory");
             build_turbo_frags<D>(p, s, hg, lane, qr, qk, tsum);
+        }
+    }
+    if constexpr (CL) {
+        float* qpj = reinterpret_cast<float*>(smem + RG::QPJ);
+        if constexpr (VG == kTurbo) turbo_qproj_slice<D>(p, s, hg, crank, qpj);
+        __syncwarp();
+        cluster_arrive();   // start barrier (with the producer warps of the cluster)
+        cluster_wait();
+        if constexpr (VG == kTurbo) {
+            turbo_qproj_gather<D>(p, crank, qpj);
+            named_sync(1, kConsumerThreads);
+            if (w == 0) build_turbo_frags<D>(p, s, hg, lane, qr, qk, tsum, qpj);
         }
     }
     if constexpr (UM) {
@@ -1318,15 +1561,23 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
             failed_at = 0;
         }
     }
-    for (int k = failed_at < 0 ? 0 : nstage; k < nstage; ++k) {
-        const int slot = k % kStages;
-        int seg, start, cnt;
-        stage_at<D>(sg, k, seg, start, cnt);
-        if (!mbar_wait(full + slot, (k / kStages) & 1, p.wait_limit)) {
+    // stage sequence of this CTA's ring: its own stages 0..nstage-1, or in
+    // cluster mode the stages named by the slot headers up to a sentinel
+    const int nloop = failed_at >= 0 ? 0 : CL ? INT_MAX : nstage;
+    for (int jj = 0; jj < nloop; ++jj) {
+        const int slot = jj % kStages;
+        if (!mbar_wait(full + slot, (jj / kStages) & 1, p.wait_limit)) {
             atomicExch(p.status, FKV_ERR_TIMEOUT);
-            failed_at = k;
+            failed_at = jj;
             break;
         }
+        int k = jj;
+        if constexpr (CL) {
+            k = *reinterpret_cast<volatile int*>(hdr + slot);
+            if (k < 0) break;   // sentinel: the cluster's stages are all taken
+        }
+        int seg, start, cnt;
+        stage_at<D>(sg, k, seg, start, cnt);
         uint8_t* kbuf = smem + slot * RG::SLOT;
         const uint8_t* vbuf = kbuf + RG::VOFF;
         const int ntile = (cnt + kTile - 1) / kTile;
@@ -1409,8 +1660,15 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
     if (failed_at >= 0) {
         // the producer runs at most kStages ahead of the consumers: wait
         // (bounded) for the copies it may still have in flight, then leave
-        for (int k = failed_at; k < min(nstage, failed_at + kStages); ++k) {
-            if (!mbar_wait(full + (k % kStages), (k / kStages) & 1)) break;
+        if constexpr (CL) {
+            for (uint32_t i = 0; i < kWaitLimit && *pdone == 0; ++i) __nanosleep(64);
+            const int iss = *issued_c;
+            for (int jj = failed_at; jj < iss; ++jj)
+                if (!mbar_wait(full + (jj % kStages), (jj / kStages) & 1)) break;
+        } else {
+            for (int k = failed_at; k < min(nstage, failed_at + kStages); ++k) {
+                if (!mbar_wait(full + (k % kStages), (k / kStages) & 1)) break;
+            }
         }
     }
 
@@ -1454,15 +1712,16 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
         }
     }
 
-    if (p.splits == 1) {
+    if (!CL && p.splits == 1) {
         merge_warps<D>(p, sh_rec, s, hg, sh_rec + kConsumerWarps * R::SIZE);
         return;
     }
 
-    // ---- CTA record -> workspace, then the last CTA of this stream merges
-    const int64_t slotrec = ((int64_t)s * p.HG + hg) * p.splits + split;
-    float* gr = p.ws + slotrec * R::SIZE;
+    // ---- CTA record -> workspace (cluster mode: this CTA's shared memory),
+    // then the last CTA of this stream merges
     float* cw = sh_rec + kConsumerWarps * R::SIZE;   // [warp][head] weights exp(m_w - M)
+    float* gr = CL ? cw + kConsumerWarps * kHeadsPerTile
+                   : p.ws + (((int64_t)s * p.HG + hg) * p.splits + split) * R::SIZE;
     if (threadIdx.x < kHeadsPerTile) {
         const int head = threadIdx.x;
         float M = -INFINITY, L = 0.f, mn = INFINITY, mf = -INFINITY;
@@ -1498,6 +1757,31 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
             acc.w = fmaf(wgt, o.w, acc.w);
         }
         *reinterpret_cast<float4*>(gr + R::O + e) = acc;
+    }
+    if constexpr (CL) {
+        named_sync(1, kConsumerThreads);
+        cluster_arrive();   // end barrier 1: every CTA record of the cluster is ready
+        cluster_wait();
+        cluster_merge<D>(p, s, hg, split, crank, gr);
+        if (p.groups > 1) __threadfence();   // the cluster's record, before rank 0's ticket
+        __syncwarp();
+        cluster_arrive();   // end barrier 2: no peer reads this CTA's shared memory any more
+        cluster_wait();
+        if (p.groups == 1 || crank != 0) return;
+        named_sync(1, kConsumerThreads);
+        if (threadIdx.x == 0) {
+            int* tk = p.tickets + ((int64_t)s * p.HG + hg);
+            const int old = atomicAdd(tk, 1);
+            sh_last = (old == p.groups - 1);
+            if (sh_last) *tk = 0;
+        }
+        named_sync(1, kConsumerThreads);
+        if (!sh_last) return;
+        __threadfence();
+        const float* gbase = p.ws + ((int64_t)s * p.HG + hg) * p.groups * R::SIZE;
+        merge_splits<D>(p, gbase, p.groups, s, hg, smem,
+                        reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR));
+        return;
     }
     __threadfence();
     named_sync(1, kConsumerThreads);
@@ -1630,6 +1914,18 @@ KernelPick pick_kernel(const FkvDecodeShape* sh, bool turbo, int nh) {
                             : KernelPick{decode_fp8_kernel<64, 32>, Ring<64, 32>::BYTES + 1024};
 }
 
+// cluster-mode instantiations (mma.sync far path, or TurboQuant)
+KernelPick pick_cl_kernel(const FkvDecodeShape* sh, bool turbo) {
+    if (turbo)
+        return sh->D == 128 ? KernelPick{decode_fp8_kernel<128, kTurbo, 0, true>, Ring<128, kTurbo>::BYTES + 1024}
+                            : KernelPick{decode_fp8_kernel<64, kTurbo, 0, true>, Ring<64, kTurbo>::BYTES + 1024};
+    if (sh->D == 128)
+        return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<128, 0, 0, true>, Ring<128, 0>::BYTES + 1024}
+                                : KernelPick{decode_fp8_kernel<128, 32, 0, true>, Ring<128, 32>::BYTES + 1024};
+    return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<64, 0, 0, true>, Ring<64, 0>::BYTES + 1024}
+                            : KernelPick{decode_fp8_kernel<64, 32, 0, true>, Ring<64, 32>::BYTES + 1024};
+}
+
 int resident_for(const FkvDecodeShape* sh, bool turbo, int nh = -1) {
     if (nh < 0) nh = um_heads(sh, turbo);
     const KernelPick k = pick_kernel(sh, turbo, nh);
@@ -1704,6 +2000,7 @@ struct Plan {
     size_t rec_bytes, ticket_bytes;
     size_t qproj_bytes;   // turbo only: (B*Hq, 2D) f32 after the counters
     int near_w, far_w;
+    int csize = 0, groups = 0;   // cluster mode (csize >= 2): CTAs per cluster, clusters per unit
 };
 
 // Cost model (measured on B200, per token): an fp16 near / decode token costs
@@ -1764,6 +2061,80 @@ Plan make_plan(const FkvDecodeShape* sh, int resident, bool turbo = false) {
     return pl;
 }
 
+// Cluster mode plan.  Small jobs (fewer (stream, head group) units than half
+// the resident CTA slots) give each unit one cluster of C CTAs, or m
+// clusters of C (C <= 16), sized so that all clusters run in one wave and
+// every CTA gets at least two ring stages; the CTAs of a cluster balance
+// their stages dynamically and merge through distributed shared memory, the
+// m cluster records of a unit (m > 1) through the workspace.  csize = 0:
+// not eligible (large job, explicit split count, or no cluster fits).
+bool cluster_mode_enabled() {
+    const char* e = std::getenv("FKV_CLUSTER");
+    return !(e != nullptr && std::strcmp(e, "0") == 0);
+}
+
+// clusters of `c` CTAs of `k` that can run at once (0 = cannot launch)
+int max_active_clusters(const KernelPick& k, int c, dim3 grid) {
+    struct Entry {
+        int dev;
+        const void* fn;
+        int c;
+        int n;
+    };
+    static thread_local std::vector<Entry> cache;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    for (const Entry& e : cache)
+        if (e.dev == dev && e.fn == (const void*)k.fn && e.c == c) return e.n;
+    int n = 0;
+    if (cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem) == cudaSuccess &&
+        cudaFuncSetAttribute(k.fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = k.smem;
+        cudaLaunchAttribute a[1];
+        a[0].id = cudaLaunchAttributeClusterDimension;
+        a[0].val.clusterDim.x = (unsigned)c;
+        a[0].val.clusterDim.y = 1;
+        a[0].val.clusterDim.z = 1;
+        cfg.attrs = a;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, k.fn, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();   // a failed query leaves no sticky error behind
+    cache.push_back(Entry{dev, (const void*)k.fn, c, n});
+    return n;
+}
+
+Plan make_cl_plan(const FkvDecodeShape* sh, bool turbo) {
+    Plan pl = make_plan(sh, 2, turbo);
+    pl.csize = pl.groups = 0;
+    if (!cluster_mode_enabled() || sh->num_splits > 0) return pl;
+    const KernelPick k = pick_cl_kernel(sh, turbo);
+    const int res = resident_ctas(k.fn, k.smem);
+    const int64_t units = (int64_t)sh->B * sh->Hk * pl.HG;
+    const int64_t slots = (int64_t)num_sms() * res;
+    if (units * 2 > slots) return pl;
+    const int64_t stages = ((int64_t)sh->n_near_alloc + 63) / 64 + ((int64_t)sh->n_far + 127) / 128 +
+                           ((int64_t)sh->n_dec + 63) / 64;
+    const int64_t T = std::min<int64_t>(slots / units, std::max<int64_t>(1, stages / 2));
+    if (T < 2) return pl;
+    int C = (int)std::min<int64_t>(T, kMaxCluster);
+    const int m = (int)std::max<int64_t>(1, std::min<int64_t>(T / C, kDirectMerge));
+    // shrink the cluster until every cluster of the launch is co-resident
+    for (; C >= 2; --C) {
+        const dim3 grid((unsigned)(C * m), (unsigned)pl.HG, (unsigned)(sh->B * sh->Hk));
+        if ((int64_t)max_active_clusters(k, C, grid) >= units * m) break;
+    }
+    if (C < 2) return pl;
+    pl.csize = C;
+    pl.groups = m;
+    pl.splits = C * m;
+    pl.rec_bytes = m > 1 ? (size_t)units * m * (40 + 8 * sh->D) * sizeof(float) : 0;
+    return pl;
+}
+
 // q heads per CTA on the tensor-core far path (0 = mma.sync path).  Eligible:
 // fp8 K with D = 128, a far tier, far rows inside the tensor map's int32
 // range.  Chosen by default when a CTA's planned work is at least
@@ -1810,7 +2181,7 @@ bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
 // Opt every kernel instantiation into its dynamic shared memory once per
 // device, then launch.
 int launch_kernel(KernelFn kern, int smem, dim3 grid, const DecodeParams& p, cudaStream_t st,
-                  const TMaps& maps, bool after_qproj = false) {
+                  const TMaps& maps, bool after_qproj = false, int cluster = 0) {
     static thread_local std::vector<std::pair<int, const void*>> done;
     int dev = 0;
     FKV_CUDA_CHECK(cudaGetDevice(&dev));
@@ -1819,7 +2190,22 @@ int launch_kernel(KernelFn kern, int smem, dim3 grid, const DecodeParams& p, cud
         FKV_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         done.push_back(key);
     }
-    if (after_qproj) {
+    if (cluster > 0) {
+        // cluster mode (attributes set by max_active_clusters when planned)
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = (unsigned)cluster;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        FKV_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, p, maps));
+    } else if (after_qproj) {
         // programmatic dependent launch: the decode grid may begin (barrier
         // set-up, first tier copies) while the q-projection kernel finishes
         cudaLaunchConfig_t cfg{};
@@ -1860,11 +2246,18 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
                             fp16_tensor_map(p.dec_v, bh * sh->dec_stride, sh->D, &maps.dec_v),
                         FKV_ERR_CUDA, "cuTensorMapEncodeTiled failed for the decode buffer");
     }
-    const KernelPick kp = pick_kernel(sh, turbo, nh);
-    const Plan pl =
-        make_plan(sh, resident_ctas(kp.fn, kp.smem, nh > 0 ? (int)UmLayout<128, 0>::TMEM_COLS : 0), turbo);
+    KernelPick kp = pick_kernel(sh, turbo, nh);
+    Plan pl = make_plan(sh, resident_ctas(kp.fn, kp.smem, nh > 0 ? (int)UmLayout<128, 0>::TMEM_COLS : 0), turbo);
+    if (nh == 0) {
+        const Plan cp = make_cl_plan(sh, turbo);
+        if (cp.csize >= 2) {
+            pl = cp;
+            kp = pick_cl_kernel(sh, turbo);
+        }
+    }
+    const bool cl = pl.csize >= 2;
     const size_t qoff = (pl.ticket_bytes + 255) & ~(size_t)255;
-    const size_t front = turbo ? qoff + pl.qproj_bytes : pl.ticket_bytes;
+    const size_t front = turbo && !cl ? qoff + pl.qproj_bytes : pl.ticket_bytes;
     const size_t need = pl.rec_bytes + front + 256;
     FKV_REQUIRE(workspace != nullptr && ws_bytes >= need, FKV_ERR_INVALID,
                 "workspace too small: %zu < %zu bytes", ws_bytes, need);
@@ -1872,6 +2265,7 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
     p.B = sh->B; p.Hq = sh->Hq; p.Hk = sh->Hk; p.G = sh->Hq / sh->Hk; p.HG = pl.HG;
     p.Np = sh->n_near_alloc; p.F = sh->n_far; p.n_dec = sh->n_dec; p.dec_stride = sh->dec_stride;
     p.splits = pl.splits; p.near_w = pl.near_w; p.far_w = pl.far_w; p.margin = sh->spike_margin;
+    p.csize = pl.csize; p.groups = pl.groups;
     p.qscale = (float)(1.0 / sqrt((double)sh->D));   // same f32 constant as the host oracle
     p.wait_limit = sh->wait_limit > 0 ? (uint32_t)sh->wait_limit : kWaitLimit;
     p.test_stall = (sh->test_flags & FKV_TEST_STALL) ? 1 : 0;
@@ -1885,6 +2279,7 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
                 "workspace too small for counters + records (%zu bytes)", ws_bytes);
     p.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + rec_off);
     dim3 grid(pl.splits, pl.HG, sh->B * sh->Hk);
+    if (cl) return launch_kernel(kp.fn, kp.smem, grid, p, st, maps, false, pl.csize);
     if (turbo) {
         float* qproj = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + qoff);
         p.qproj = qproj;
@@ -1936,8 +2331,11 @@ size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s) {
     // (and for either q.K path of the fp8 tier)
     const Plan a = make_plan(s, resident_for(s, false)), b = make_plan(s, resident_for(s, true), true);
     const Plan c = make_plan(s, resident_for(s, false, 0));
+    const Plan d = make_cl_plan(s, false), e = make_cl_plan(s, true);
     const Plan& ab = a.rec_bytes >= b.rec_bytes ? a : b;
-    const Plan& pl = ab.rec_bytes >= c.rec_bytes ? ab : c;
+    const Plan& de = d.rec_bytes >= e.rec_bytes ? d : e;
+    const Plan& abd = ab.rec_bytes >= de.rec_bytes ? ab : de;
+    const Plan& pl = abd.rec_bytes >= c.rec_bytes ? abd : c;
     return pl.rec_bytes + pl.ticket_bytes + 256 + ((pl.qproj_bytes + 255) & ~(size_t)255) + 256;
 }
 
@@ -1953,6 +2351,32 @@ int fkv_decode_status(const void* workspace, int32_t* status, int32_t clear, voi
     if (clear && word != 0)
         FKV_CUDA_CHECK(cudaMemsetAsync(const_cast<void*>(workspace), 0, sizeof(word), st));
     *status = word;
+    return FKV_OK;
+}
+
+int fkv_decode_plan(const FkvDecodeShape* sh, const uint8_t* far_k, int32_t turbo, int32_t* out) {
+    fkv::clear_error();
+    const int rc = validate(sh);
+    if (rc) return rc;
+    FKV_REQUIRE(out != nullptr, FKV_ERR_INVALID, "fkv_decode_plan: out is NULL");
+    int nh = turbo ? 0 : um_heads(sh, false);
+    if (nh > 0) {
+        CUtensorMap m;
+        if (far_k == nullptr || !aligned16(far_k) ||
+            !far_k_tensor_map(far_k, (int64_t)sh->B * sh->Hk * sh->n_far, sh->D, &m))
+            nh = 0;
+    }
+    const KernelPick kp = pick_kernel(sh, turbo != 0, nh);
+    Plan pl = make_plan(sh, resident_ctas(kp.fn, kp.smem, nh > 0 ? (int)UmLayout<128, 0>::TMEM_COLS : 0),
+                        turbo != 0);
+    if (nh == 0) {
+        const Plan cp = make_cl_plan(sh, turbo != 0);
+        if (cp.csize >= 2) pl = cp;
+    }
+    out[0] = nh;
+    out[1] = pl.splits;
+    out[2] = pl.csize;
+    out[3] = pl.groups;
     return FKV_OK;
 }
 
@@ -2149,7 +2573,9 @@ extern "C" int fkv_decode_fp8_noalloc(const FkvDecodeShape* sh, const uint16_t* 
     // mma.sync when far_k has no tensor map): accept only shapes whose
     // scratch fits for both, so the check below is the exact limit
     const Plan pa = make_plan(sh, resident_for(sh, false)), pb = make_plan(sh, resident_for(sh, false, 0));
-    const Plan& pl = pa.rec_bytes + pa.ticket_bytes >= pb.rec_bytes + pb.ticket_bytes ? pa : pb;
+    const Plan pc = make_cl_plan(sh, false);
+    const Plan& pab = pa.rec_bytes + pa.ticket_bytes >= pb.rec_bytes + pb.ticket_bytes ? pa : pb;
+    const Plan& pl = pab.rec_bytes + pab.ticket_bytes >= pc.rec_bytes + pc.ticket_bytes ? pab : pc;
     const size_t need = pl.rec_bytes + pl.ticket_bytes + 256;
     FKV_REQUIRE(need <= kNoAllocScratchBytes, FKV_ERR_INVALID,
                 "fkv_decode_fp8_noalloc: shape needs %zu scratch bytes, above the fixed "

@@ -187,6 +187,16 @@ int fkv_decode_status(const void* workspace, int32_t* status, int32_t clear, voi
  * FKV_QK_PATH=tcgen05 forces either path where the shape allows it. */
 int fkv_decode_qk_path(const FkvDecodeShape* s, const uint8_t* far_k);
 
+/* How a decode call of this shape is launched (no counterpart in the
+ * reference): out[0] = q heads per CTA on the tensor-core q.K path (0 =
+ * mma.sync), out[1] = CTAs per (b, kv head, group of 8 q heads), out[2] =
+ * thread-block cluster size (0 = no clusters: split records merged through
+ * the workspace; >= 2 = the CTAs of a cluster share the stream's stages
+ * dynamically and merge through distributed shared memory), out[3] =
+ * clusters per (b, kv head, head group).  turbo != 0 for fkv_decode_turbo.
+ * FKV_CLUSTER=0 in the environment disables the cluster mode. */
+int fkv_decode_plan(const FkvDecodeShape* s, const uint8_t* far_k, int32_t turbo, int32_t* out);
+
 /* TurboQuant far tier, scores directly on codes.  Replaces
  * TurboFoveatedHandle::operator() (csrc/foveated_attn.cpp:407-491) and kernel
  * foveated_2tier_turbo (csrc/kernels/foveated_attn.metal:559-767); the

@@ -55,6 +55,38 @@ def qk_path(request, monkeypatch):
     return request.param
 
 
+@pytest.fixture(params=["tcgen05", "mma_cluster", "mma_flat"])
+def launch_mode(request, monkeypatch):
+    """q.K path and, on the mma.sync path, the cluster mode (CTAs of a
+    stream share its stages dynamically and merge through distributed shared
+    memory) or the flat split with workspace records (FKV_CLUSTER=0)."""
+    path, _, flat = request.param.partition("_")
+    monkeypatch.setenv("FKV_QK_PATH", "tcgen05" if path == "tcgen05" else "mma")
+    monkeypatch.setenv("FKV_CLUSTER", "0" if flat == "flat" else "1")
+    return request.param
+
+
+def _plan(lay, Hq, turbo=False):
+    import ctypes as C
+    from foveated_kv_b200 import _native
+    out = (C.c_int32 * 4)()
+    sh = lay._fill_shape(Hq, lay.spike_margin)
+    far = lay.far_k.data_ptr() if lay.far_k is not None and lay.far_k.numel() else None
+    _native.check(_native.load().fkv_decode_plan(C.byref(sh), far, int(turbo), out), "plan")
+    return list(out)
+
+
+def _check_mode(lay, Hq, mode, turbo=False):
+    nh, splits, csize, groups = _plan(lay, Hq, turbo)
+    if mode == "tcgen05":
+        assert nh > 0
+    elif mode == "mma_cluster":
+        assert nh == 0 and csize >= 2, (nh, splits, csize, groups)
+    elif mode == "mma_flat":
+        assert nh == 0 and csize == 0
+    return nh, splits, csize, groups
+
+
 def _decode_and_check(lay, w, margin, name, tc=None):
     t_q = torch.from_numpy(w["q"]).cuda()
     out, fl, tk = lay.attend_fused_with_spikes(t_q)
@@ -107,26 +139,31 @@ def test_c3_slice_decode_with_spikes(c3_slice, qk_path):
 # ---- c1 at 4K and 16K ----------------------------------------------------------------
 
 @pytest.mark.parametrize("name", ["c1_4k", "c1_16k"])
-def test_c1_decode(name, qk_path):
+def test_c1_decode(name, launch_mode):
     c = _cfg(name)
     w = numpy_workload(72, c["B"], c["Hk"], c["Hq"], c["S"], c["D"], 0)
     t = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
     lay = compress_layer(t["k"], t["v"], _tier_cfg(c))
-    err, cos, _, _ = _decode_and_check(lay, w, 0.5, f"{name} ({qk_path})")
-    print(f"{name} {qk_path}: max-abs {err:.2e} cos {cos:.7f}")
+    plan = _check_mode(lay, c["Hq"], launch_mode)
+    err, cos, _, _ = _decode_and_check(lay, w, 0.5, f"{name} ({launch_mode})")
+    print(f"{name} {launch_mode} plan {plan}: max-abs {err:.2e} cos {cos:.7f}")
 
 
 # ---- c2: TurboQuant at 16K ------------------------------------------------------------
 
-def test_c2_turbo_decode_16k():
+@pytest.mark.parametrize("mode", ["cluster", "flat"])
+def test_c2_turbo_decode_16k(mode, monkeypatch):
+    monkeypatch.setenv("FKV_CLUSTER", "0" if mode == "flat" else "1")
     c = _cfg("c2")
     w = numpy_workload(73, c["B"], c["Hk"], c["Hq"], c["S"], c["D"], 0)
     t = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
     lay = compress_layer(t["k"], t["v"], _tier_cfg(c))
+    plan = _plan(lay, c["Hq"], turbo=True)
+    assert (plan[2] >= 2) == (mode == "cluster"), plan
     pi, s, cen, bnd = host_constants(c["D"])
     tc = {"Pi": pi, "S": s, "centroids": cen, "boundaries": bnd}
-    err, cos, _, _ = _decode_and_check(lay, w, 0.5, "c2 turbo 16K", tc)
-    print(f"c2: max-abs {err:.2e} cos {cos:.7f}")
+    err, cos, _, _ = _decode_and_check(lay, w, 0.5, f"c2 turbo 16K ({mode})", tc)
+    print(f"c2 {mode} plan {plan}: max-abs {err:.2e} cos {cos:.7f}")
 
 
 # ---- c4: long sequence split into 8 shards on one GPU ------------------------------

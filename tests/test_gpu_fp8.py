@@ -84,12 +84,16 @@ DECODE_CASES = [
 ]
 
 
-@pytest.fixture(params=["tcgen05", "mma"])
+@pytest.fixture(params=["tcgen05", "mma", "mma_flat"])
 def qk_path(request, monkeypatch):
     """Run a decode test on each far-tier q.K path: tcgen05 (tensor memory,
     forced with FKV_QK_PATH=tcgen05 where the shape allows it) and mma.sync
-    (FKV_QK_PATH=mma).  The default picks one per shape by CTA work size."""
-    monkeypatch.setenv("FKV_QK_PATH", request.param)
+    (FKV_QK_PATH=mma).  The default picks one per shape by CTA work size.
+    On the mma.sync path small shapes run in cluster mode (the CTAs of a
+    stream share its stages and merge through distributed shared memory);
+    mma_flat turns it off (FKV_CLUSTER=0: split records in the workspace)."""
+    monkeypatch.setenv("FKV_QK_PATH", "tcgen05" if request.param == "tcgen05" else "mma")
+    monkeypatch.setenv("FKV_CLUSTER", "0" if request.param == "mma_flat" else "1")
     return request.param
 
 

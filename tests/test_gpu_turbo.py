@@ -28,8 +28,10 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("mode", ["cluster", "flat"])
 @pytest.mark.parametrize("name,B,Hk,Hq,S,D,n_dec,kw,margin", CASES)
-def test_turbo_compress_and_decode(name, B, Hk, Hq, S, D, n_dec, kw, margin):
+def test_turbo_compress_and_decode(name, B, Hk, Hq, S, D, n_dec, kw, margin, mode, monkeypatch):
+    monkeypatch.setenv("FKV_CLUSTER", "0" if mode == "flat" else "1")
     w = numpy_workload(61, B, Hk, Hq, S, D, n_dec)
     t = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
     cfg = TierConfig(compress_method="turbo", spike_margin=margin, **kw)
