@@ -52,6 +52,10 @@ def parse():
     ap.add_argument("--batch", type=int, default=0, help="override sequences per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sdpa", action="store_true", help="skip the fp16 SDPA comparison")
+    ap.add_argument("--no-promo", action="store_true",
+                    help="skip the c3 decode-step-with-promotion measurement")
+    ap.add_argument("--promo-budget", type=int, default=0,
+                    help="records per drain in the promotion step (0: one per (b, kv head))")
     ap.add_argument("--sdpa-flashinfer", action="store_true",
                     help="also time flashinfer's decode (JIT-compiles on first use)")
     return ap.parse_args()
@@ -324,13 +328,112 @@ def qk_path_name(lay, Hq: int) -> str:
     sh = lay._fill_shape(Hq, lay.spike_margin)
     far = lay.far_k.data_ptr() if (not turbo and lay.far_k is not None and lay.far_k.numel()) else None
     out = (C.c_int32 * 4)()
-    _native.check(lib.fkv_decode_plan(C.byref(sh), far, int(turbo), out), "fkv_decode_plan")
+    try:
+        fn = lib.fkv_decode_plan
+    except AttributeError:
+        return "unknown (library without fkv_decode_plan)"
+    _native.check(fn(C.byref(sh), far, int(turbo), out), "fkv_decode_plan")
     nh, splits, csize, groups = list(out)
     path = (f"tcgen05.mma f8f6f4 ({nh} q heads/CTA)" if nh > 0 else
             "mma.sync (TurboQuant codes)" if turbo else "mma.sync")
     launch = (f"{splits} CTAs/stream in {groups} cluster(s) of {csize} (dynamic stages, DSMEM merge)"
               if csize >= 2 else f"{splits} CTAs/stream (workspace merge)")
     return f"{path}; {launch}"
+
+
+def promotion_step_bench(cfgname, device, steps, warmup, budget, batch=0, rounds=8, frac=0.01):
+    """Decode steps with the promotion loop in the timed region (config c3:
+    "each step forces 1% of far tokens per head to spike ... promotion of exact
+    fp16 rows from a pinned host archive into near headroom").
+
+    Set-up: a pool of `rounds` x 1% far positions per (b, kv head) gets spike
+    keys (3 sqrt(D) times the group's unit mean query) before compression, so
+    the archive holds their exact fp16 rows; then all but round 0 are turned
+    off in the far tier (E4M3 code 0).  Step t switches round t-1 off and
+    round t % rounds on (a fresh 1% of spiking far tokens each step), runs the
+    fused decode, reads flags/tokens back, drains them through the
+    PromotionPipeline (cooldown 5, `budget` records per drain) and makes the
+    stream wait for the batched promotion (flush).  Timed with CUDA events
+    around whole steps, host work included."""
+    import torch
+    from foveated_kv_b200 import TierConfig, compress_layer, PromotionPipeline
+    from foveated_kv_b200.synthetic import torch_workload, CONFIGS
+    c = dict(CONFIGS[cfgname])
+    if batch:
+        c["B"] = batch
+    B, Hq, Hk, D, S = c["B"], c["Hq"], c["Hk"], c["D"], c["S"]
+    cfg = TierConfig(near_pct=c["near_pct"], n_sinks=c["n_sinks"], window_size=c["window_size"],
+                     v_group=c["v_group"], spike_margin=0.5)
+    tb = cfg.tier_boundaries(S)
+    F, ms0 = tb["far_count"], tb["mid_start"]
+    n = max(1, int(F * frac))
+    w = torch_workload(3000, B, Hk, Hq, S, D, 0, device)
+    g = torch.Generator(device=device)
+    g.manual_seed(3001)
+    pool = torch.rand((B, Hk, F), generator=g, device=device).topk(rounds * n, dim=-1).indices
+    pool = pool.view(B, Hk, rounds, n)
+    qm = w["q"].float().reshape(B, Hk, Hq // Hk, D).mean(2)
+    qm = qm / qm.norm(dim=-1, keepdim=True)
+    key = (3.0 * D ** 0.5 * qm).to(torch.float16)
+    bi = torch.arange(B, device=device)[:, None, None]
+    hi = torch.arange(Hk, device=device)[None, :, None]
+    pos = (ms0 + pool).view(B, Hk, rounds * n)
+    w["k"][bi, hi, pos] = key[:, :, None, :]
+    lay = compress_layer(w["k"], w["v"], cfg)
+    q = w["q"]
+    del w
+    code = lay.far_k[bi[:, :, 0], hi[:, :, 0], pool[:, :, 0, 0]].clone()     # (B, Hk, D)
+    for r in range(1, rounds):
+        lay.far_k[bi, hi, pool[:, :, r]] = 0
+    arc_k = lay.archive_k.cpu().pin_memory()
+    arc_v = lay.archive_v.cpu().pin_memory()
+    lay.archive_k = lay.archive_v = None
+    torch.cuda.empty_cache()
+    pipe = PromotionPipeline(1, cooldown_steps=5, max_per_drain=budget)
+    pipe.register_archive_host(0, arc_k, arc_v, lay.far_idx)
+    pipe.register_blob(0, lay.get_blob_info())
+    nv0 = int(lay.near_valid.sum().item())
+    fl_h = torch.empty((B, Hq), dtype=torch.int32).pin_memory()
+    tk_h = torch.empty((B, Hq), dtype=torch.int32).pin_memory()
+    st = torch.cuda.current_stream()
+
+    def step(t):
+        r, rp = t % rounds, (t - 1) % rounds
+        if rp != r:
+            lay.far_k[bi, hi, pool[:, :, rp]] = 0
+            lay.far_k[bi, hi, pool[:, :, r]] = code[:, :, None, :]
+        _, fl, tk = lay.attend_fused_with_spikes(q)
+        fl_h.copy_(fl, non_blocking=True)
+        tk_h.copy_(tk, non_blocking=True)
+        st.synchronize()
+        queued = pipe.drain_spikes(0, fl_h.numpy(), tk_h.numpy(), lay.far_idx, t)
+        pipe.flush(st)
+        return queued
+
+    for t in range(max(warmup, 3)):
+        step(t)
+    torch.cuda.synchronize()
+    before = pipe.get_stats()
+    nv_before = int(lay.near_valid.sum().item())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    t0 = max(warmup, 3)
+    queued = [step(t0 + i) for i in range(steps)]
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    after = pipe.get_stats()
+    nv_after = int(lay.near_valid.sum().item())
+    lay.check_decode()
+    done = after["promotions_completed"] - before["promotions_completed"]
+    assert nv_after - nv_before == done, (nv_after - nv_before, done)
+    pipe.close()
+    return {"ms_per_step": ms, "promotions_per_step": done / steps,
+            "queued_per_step_max": max(queued), "budget_per_drain": budget, "cooldown_steps": 5,
+            "spikes_per_stream_per_step": n, "rows_promoted_total": nv_after - nv0,
+            "headroom_full": after["promotions_headroom_full"],
+            "what": "per step: re-inject 1% spikes, fused decode, D2H flags/tokens, drain "
+                    "(PromotionPipeline), batched H2D of exact fp16 rows + scatter kernel, flush"}
 
 
 def main_seqsplit(args, rank, world, device):
@@ -566,6 +669,13 @@ def main():
     compress_ms = layers[0].compress_ms
     del layers, outs, graph
     torch.cuda.empty_cache()
+    promo = None
+    if args.config == "c3" and world == 1 and not args.no_promo:
+        budget = args.promo_budget or B * Hk
+        promo = promotion_step_bench("c3", device, min(args.steps, 30), args.warmup, budget,
+                                     args.batch)
+        promo["decode_only_ms"] = ms
+        torch.cuda.empty_cache()
     sdpa = None
     if not args.no_sdpa and rank == 0:
         c_full = dict(c)
@@ -617,6 +727,7 @@ def main():
             "compress_gbs": (lay.memory_bytes()["total_with_archive"] +
                              B * Hk * c["S"] * D * 4) / (compress_ms * 1e-3) / 1e9,
             "sdpa_fp16": sdpa,
+            "promotion_step": promo,
             "gpu_launches": args.steps * n_layers,
             "layers_per_graph": n_layers,
             "clocks": clk.summary(),

@@ -99,9 +99,12 @@ _lib = None
 _lock = threading.Lock()
 
 
-def load(path: str = LIB_PATH):
-    """Load libfkv.so once; raises FkvNativeError if it is absent or broken."""
+def load(path: str = None):
+    """Load libfkv.so once; raises FkvNativeError if it is absent or broken.
+    FKV_LIBRARY in the environment names another build of the library (for
+    A/B timing of builds; entry points it lacks raise when used)."""
     global _lib
+    path = path or os.environ.get("FKV_LIBRARY") or LIB_PATH
     with _lock:
         if _lib is not None:
             return _lib
@@ -121,7 +124,7 @@ def load(path: str = LIB_PATH):
                 continue
             fn.restype = res
             fn.argtypes = args
-        if missing:
+        if missing and path == LIB_PATH:
             raise FkvNativeError(f"{path} lacks symbols: {missing}")
         _lib = lib
         return lib

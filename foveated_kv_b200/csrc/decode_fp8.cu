@@ -414,7 +414,7 @@ __device__ __forceinline__ void load_far_v(const uint8_t* __restrict__ vbuf, con
 // Masking, spike tracking, online softmax and the P.V product of NT far
 // tiles whose raw scores `sv` are in the S C-fragment layout (lane (r, c):
 // head r, tokens u0[t] + {2c, 2c+1, 8+2c, 9+2c}) and whose V words are in vr.
-template <int D, int VG, int NT>
+template <int D, int VG, int NT, bool CL = false>
 __device__ __forceinline__ void far_tail(const float (&sv)[4 * NT],
                                          const uint32_t (&vr)[NT][4][(D / 16 + 3) / 4],
                                          const int (&u0)[NT], int cnt, int gbase, int lane,
@@ -433,16 +433,16 @@ __device__ __forceinline__ void far_tail(const float (&sv)[4 * NT],
     }
     // spike tracker: the lane's values are in token order, so the earliest
     // index of a new strict maximum is the first j holding it (rare branch)
-    // (stages may arrive out of token order in cluster mode: an equal
+    // (stages may arrive out of token order in cluster mode: there an equal
     // maximum replaces the tracked one when its index is lower)
-    if (lm >= st.mf && lm != -INFINITY) {
+    if (CL ? (lm >= st.mf && lm != -INFINITY) : lm > st.mf) {
         int jj = 0;
 #pragma unroll
         for (int j = 4 * NT - 1; j >= 0; --j)
             if (s[j] == lm) jj = j;
         const int ut = (NT > 1 && jj >= 4) ? u0[NT - 1] : u0[0];
         const int idx = gbase + ut + ((jj & 3) >> 1) * 8 + 2 * c + (jj & 1);
-        if (lm > st.mf || idx < st.af) {
+        if (!CL || lm > st.mf || idx < st.af) {
             st.mf = lm;
             st.af = idx;
         }
@@ -504,7 +504,7 @@ __device__ __forceinline__ void far_tail(const float (&sv)[4 * NT],
 // (the tiles' loads, conversions and tensor-core products are interleaved and
 // share one online-softmax step, which gives each warp instruction-level
 // parallelism at the occupancy the register budget allows)
-template <int D, int VG, int NT>
+template <int D, int VG, int NT, bool CL = false>
 __device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
                                           const uint8_t* __restrict__ vbuf, const int (&u0)[NT],
                                           int cnt, int gbase, int lane,
@@ -559,7 +559,7 @@ __device__ __forceinline__ void far_tiles(const uint8_t* __restrict__ kbuf,
     for (int t = 0; t < NT; ++t)
 #pragma unroll
         for (int j = 0; j < 4; ++j) sv[4 * t + j] = sc[t][j >> 1][j & 1] + sc[t][j >> 1][2 + (j & 1)];
-    far_tail<D, VG, NT>(sv, vr, u0, cnt, gbase, lane, sz, st);
+    far_tail<D, VG, NT, CL>(sv, vr, u0, cnt, gbase, lane, sz, st);
 }
 
 // ---- far tiles scored on the 5th-generation tensor cores (tcgen05) ----
@@ -744,7 +744,7 @@ __device__ __forceinline__ void load_turbo_sz(const uint16_t* __restrict__ nm,
 // {0,1} f16 pairs: bit 0 and bit 16 of x -> 0x3C00 (1.0) in the matching half
 __device__ __forceinline__ uint32_t bits2_to_h2(uint32_t x) { return (x & 0x00010001u) * 0x3C00u; }
 
-template <int D>
+template <int D, bool CL = false>
 __device__ __forceinline__ void turbo_tile(const uint8_t* __restrict__ sgn,
                                            const uint8_t* __restrict__ kbuf,
                                            const uint8_t* __restrict__ vbuf, int u0, int cnt,
@@ -809,7 +809,7 @@ __device__ __forceinline__ void turbo_tile(const uint8_t* __restrict__ sgn,
         const float qjl = cf[4] * f.y * fmaf(2.f, sgn, -sum_k);
         const float v = fmaf(f.x, mse, qjl) * cf[5];
         s[j] = u < cnt ? v : -INFINITY;
-        if (u < cnt && (v > st.mf || (v == st.mf && gbase + u < st.af))) {
+        if (u < cnt && (v > st.mf || (CL && v == st.mf && gbase + u < st.af))) {
             st.mf = v;
             st.af = gbase + u;
         }
@@ -866,7 +866,7 @@ __device__ __forceinline__ void turbo_qproj_slice(const DecodeParams& p, int s, 
         if (g < p.G) {
             const uint16_t* qrow = p.q + ((int64_t)b * p.Hq + (int64_t)h * p.G + g) * D;
             const float* mrow = col < D ? p.turbo_pi + (int64_t)col * D : p.turbo_s + (int64_t)(col - D) * D;
-#pragma unroll 4
+#pragma unroll
             for (int i = 0; i < D; i += 8) {
                 const uint4 qw = __ldg(reinterpret_cast<const uint4*>(qrow + i));
                 const float4 m0 = __ldg(reinterpret_cast<const float4*>(mrow + i));
@@ -888,9 +888,18 @@ __device__ __forceinline__ void turbo_qproj_gather(const DecodeParams& p, int cr
                                                    float* __restrict__ qpj) {
     const int C = p.csize;
     const int cw = (2 * D + C - 1) / C;
-    for (int idx = threadIdx.x; idx < kHeadsPerTile * 2 * D; idx += kConsumerThreads) {
+    constexpr int PER = kHeadsPerTile * 2 * D / kConsumerThreads;
+    float v[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {   // every load issued before the first store
+        const int idx = (int)threadIdx.x + i * kConsumerThreads;
         const int owner = (idx % (2 * D)) / cw;
-        if (owner != crank) qpj[idx] = ld_peer_f32(peer_smem(qpj + idx, (uint32_t)owner));
+        v[i] = owner != crank ? ld_peer_f32(peer_smem(qpj + idx, (uint32_t)owner)) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+        const int idx = (int)threadIdx.x + i * kConsumerThreads;
+        if ((idx % (2 * D)) / cw != crank) qpj[idx] = v[i];
     }
 }
 
@@ -1220,7 +1229,7 @@ __device__ __forceinline__ void cluster_merge(const DecodeParams& p, int s, int 
 // take more stages; the CTA records are then merged through distributed
 // shared memory instead of global records and a ticket.
 template <int D, int VG, int NH = 0, bool CL = false>
-__global__ void __maxnreg__(NH > 0 ? 128 : 136)
+__global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
     decode_fp8_kernel(const DecodeParams p, const __grid_constant__ TMaps maps) {
     using R = RecLayout<D>;
     using RG = Ring<D, VG>;
@@ -1459,14 +1468,18 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
                 cluster_arrive();   // start barrier: rank 0's counter is set, every CTA runs
                 cluster_wait();
                 if (lane == 0) {
+                    // each claim is made one stage ahead, so the round trip to
+                    // rank 0 overlaps the wait for the next free slot
                     const uint32_t ctr = peer_smem(smem + RG::COUNTER, 0);
+                    int k_next = done ? nstage : (int)atom_add_peer(ctr, 1u);
                     while (!done) {
                         const int slot = j % kStages;
                         if (!mbar_wait(empty + slot, ((j / kStages) - 1) & 1, p.wait_limit)) {
                             atomicExch(p.status, FKV_ERR_TIMEOUT);
                             break;
                         }
-                        const int k = (int)atom_add_peer(ctr, 1u);
+                        const int k = k_next;
+                        if (k < nstage) k_next = (int)atom_add_peer(ctr, 1u);
                         hdr[slot] = k < nstage ? k : -1;
                         if (k < nstage) {
                             issue(k, slot);
@@ -1566,18 +1579,21 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
     const int nloop = failed_at >= 0 ? 0 : CL ? INT_MAX : nstage;
     for (int jj = 0; jj < nloop; ++jj) {
         const int slot = jj % kStages;
-        if (!mbar_wait(full + slot, (jj / kStages) & 1, p.wait_limit)) {
+        int k = jj;
+        int seg, start, cnt;
+        if constexpr (!CL) stage_at<D>(sg, k, seg, start, cnt);
+        // (outside cluster mode the consumers' data waits keep the fixed
+        // limit; the stall test never reaches them)
+        if (!mbar_wait(full + slot, (jj / kStages) & 1, CL ? p.wait_limit : kWaitLimit)) {
             atomicExch(p.status, FKV_ERR_TIMEOUT);
             failed_at = jj;
             break;
         }
-        int k = jj;
         if constexpr (CL) {
             k = *reinterpret_cast<volatile int*>(hdr + slot);
             if (k < 0) break;   // sentinel: the cluster's stages are all taken
+            stage_at<D>(sg, k, seg, start, cnt);
         }
-        int seg, start, cnt;
-        stage_at<D>(sg, k, seg, start, cnt);
         uint8_t* kbuf = smem + slot * RG::SLOT;
         const uint8_t* vbuf = kbuf + RG::VOFF;
         const int ntile = (cnt + kTile - 1) / kTile;
@@ -1598,13 +1614,13 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
                     load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
                     load_sz<D, VG>(sc, ze, u0[1], cnt, lane, sz[1]);
                     ok = far_tiles_um<D, VG, 2, NH>(kbuf, vbuf, u0, cnt, start, lane, w, ta, escale, mmab,
-                                                    par, p.wait_limit, sz, st);
+                                                    par, kWaitLimit, sz, st);
                 } else if (32 * w < cnt) {
                     const int u0[1] = {32 * w};
                     uint32_t sz[1][4];
                     load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
                     ok = far_tiles_um<D, VG, 1, NH>(kbuf, vbuf, u0, cnt, start, lane, w, ta, escale, mmab,
-                                                    par, p.wait_limit, sz, st);
+                                                    par, kWaitLimit, sz, st);
                 }
             }
             if (!ok) {
@@ -1630,7 +1646,7 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
                     if (i < ntile) {
                         uint32_t ng[4], vs2[2];
                         load_turbo_sz<D>(nm, gm, vsp, i * kTile, cnt, lane, ng, vs2);
-                        turbo_tile<D>(sgn, kbuf, vbuf, i * kTile, cnt, srow0, start, lane, qr, qk,
+                        turbo_tile<D, CL>(sgn, kbuf, vbuf, i * kTile, cnt, srow0, start, lane, qr, qk,
                                       cf, sum_r, sum_k, ng, vs2, st);
                     }
                 }
@@ -1643,12 +1659,12 @@ __global__ void __maxnreg__(NH > 0 ? 128 : 136)
                     uint32_t sz[2][4];
                     load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
                     load_sz<D, VG>(sc, ze, u0[1], cnt, lane, sz[1]);
-                    far_tiles<D, VG, 2>(kbuf, vbuf, u0, cnt, start, lane, qs, sz, st);
+                    far_tiles<D, VG, 2, CL>(kbuf, vbuf, u0, cnt, start, lane, qs, sz, st);
                 } else if (w < ntile) {
                     const int u0[1] = {w * kTile};
                     uint32_t sz[1][4];
                     load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
-                    far_tiles<D, VG, 1>(kbuf, vbuf, u0, cnt, start, lane, qs, sz, st);
+                    far_tiles<D, VG, 1, CL>(kbuf, vbuf, u0, cnt, start, lane, qs, sz, st);
                 }
             }
         } else if (w < ntile) {
@@ -2069,8 +2085,10 @@ Plan make_plan(const FkvDecodeShape* sh, int resident, bool turbo = false) {
 // m cluster records of a unit (m > 1) through the workspace.  csize = 0:
 // not eligible (large job, explicit split count, or no cluster fits).
 bool cluster_mode_enabled() {
+    // opt-in (FKV_CLUSTER=1): on B200 the flat split measured faster for
+    // every benchmarked shape (the cluster placement leaves SMs idle)
     const char* e = std::getenv("FKV_CLUSTER");
-    return !(e != nullptr && std::strcmp(e, "0") == 0);
+    return e != nullptr && std::strcmp(e, "1") == 0;
 }
 
 // clusters of `c` CTAs of `k` that can run at once (0 = cannot launch)

@@ -4,12 +4,21 @@
 #include <cstdio>
 #include <string>
 
+#include <cuda_runtime.h>
+#include <cstdint>
+
 #include "../../include/fkv.h"
 
 namespace fkv {
 
 void set_error(const char* fmt, ...);
 void clear_error();
+
+// Batched promotion scatter (promo_scatter.cu): `stage` is a device copy of
+// [K rows n*D | V rows n*D] fp16, destination rows n int64 (row index into
+// near_k / near_v), then m (near_valid index, new count) int32 pairs.
+int promo_scatter(const void* stage, int n, int m, int D, uint16_t* near_k, uint16_t* near_v,
+                  int32_t* near_valid, cudaStream_t st);
 
 }  // namespace fkv
 

@@ -3,13 +3,16 @@
 // Host side of the closed loop of the reference's PromotionPipeline
 // (csrc/promotion_pipeline.cpp:20-248): drain_spikes filters the fused
 // kernel's per-head spike flags (GQA dedup, cooldown, position dedup, budget)
-// and queues records; one worker std::thread per pipeline copies the exact
-// fp16 K/V rows of each record from a host archive (mmapped file or caller
-// memory) through pinned staging into slot near_valid[b, h] of the device
-// near tier with cudaMemcpyAsync on its own stream, then writes the new count
-// with a second copy on the same stream.  Stream order makes the count visible
-// only after the row it covers, so a decode launch that reads near_valid sees
-// either the old count or the new count with its row in place.
+// and queues records; one worker std::thread per pipeline takes everything
+// queued at once, packs the exact fp16 K/V rows of those records from the
+// host archive (mmapped file or caller memory) into one pinned staging buffer
+// together with their destination slots (near_valid[b, h], counted on a host
+// shadow) and the new counts, moves the batch to the device with ONE
+// cudaMemcpyAsync on its own stream, and launches a scatter kernel that writes
+// the rows, then a second one that stores the counts.  Stream order makes a
+// count visible only after the rows it covers, so a decode launch that reads
+// near_valid sees either the old count or the new count with its rows in
+// place.
 //
 // Differences from the reference, all identical at B = 1: near_valid is per
 // (b, kv head) and GQA dedup / cooldown / position dedup are keyed by batch
@@ -21,6 +24,7 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <atomic>
 #include <chrono>
 #include <condition_variable>
@@ -60,7 +64,7 @@ struct Blob {
     std::vector<int32_t> shadow;   // host copy of near_valid; the worker is its only writer
 };
 
-constexpr int kStagingSlots = 64;
+constexpr int kStagingBufs = 2;   // pinned batch buffers in flight
 
 }  // namespace
 
@@ -81,34 +85,39 @@ struct FkvPromo {
     std::atomic<uint64_t> detected{0}, queued{0}, deduplicated{0}, cooled{0}, completed{0},
         headroom_full{0};
 
-    // device resources, created by the worker on first use
+    // device resources, created by the worker on first use: its stream,
+    // kStagingBufs pinned batch buffers (each reused once the copy out of it
+    // has completed) and one device staging buffer (reused in stream order)
     bool cuda_ready = false;
     cudaStream_t stream = nullptr;
     cudaEvent_t done = nullptr;
-    uint8_t* staging = nullptr;                 // pinned, kStagingSlots slots
-    size_t slot_bytes = 0;
-    cudaEvent_t slot_ev[kStagingSlots] = {};
-    int next_slot = 0;
+    uint8_t* staging[kStagingBufs] = {};
+    size_t staging_bytes[kStagingBufs] = {};
+    cudaEvent_t staging_ev[kStagingBufs] = {};
+    int next_buf = 0;
+    void* dev_stage = nullptr;
+    size_t dev_stage_bytes = 0;
     std::string worker_error;
 
     ~FkvPromo();
     void run();
-    bool ensure_cuda(size_t need_slot_bytes);
-    void promote(const Record& r);
+    bool ensure_cuda();
+    void promote_batch(std::vector<Record>& batch);
+    void promote_layer(int layer, const Record* recs, size_t n);
 };
 
 void FkvPromo::run() {
     while (true) {
-        Record r;
+        std::vector<Record> batch;
         {
             std::unique_lock<std::mutex> lk(mu);
             cv.wait(lk, [&] { return !queue.empty() || !running.load(); });
             if (queue.empty()) break;   // stopping and drained
-            r = queue.front();
-            queue.pop_front();
+            batch.assign(queue.begin(), queue.end());
+            queue.clear();
             busy = true;
         }
-        promote(r);
+        promote_batch(batch);
         {
             std::lock_guard<std::mutex> lk(mu);
             busy = false;
@@ -118,61 +127,115 @@ void FkvPromo::run() {
     idle_cv.notify_all();
 }
 
-bool FkvPromo::ensure_cuda(size_t need) {
-    if (cuda_ready && need <= slot_bytes) return true;
+bool FkvPromo::ensure_cuda() {
+    if (cuda_ready) return true;
     if (cudaSetDevice(device) != cudaSuccess) return false;
-    if (!cuda_ready) {
-        if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess) return false;
-        if (cudaEventCreateWithFlags(&done, cudaEventDisableTiming) != cudaSuccess) return false;
-        for (auto& e : slot_ev)
-            if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return false;
-    }
-    if (need > slot_bytes) {
-        cudaStreamSynchronize(stream);
-        if (staging) cudaFreeHost(staging);
-        slot_bytes = (need + 255) & ~(size_t)255;
-        if (cudaHostAlloc((void**)&staging, slot_bytes * kStagingSlots, cudaHostAllocDefault) !=
-            cudaSuccess) {
-            staging = nullptr;
-            slot_bytes = 0;
-            return false;
-        }
-    }
+    if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess) return false;
+    if (cudaEventCreateWithFlags(&done, cudaEventDisableTiming) != cudaSuccess) return false;
+    for (auto& e : staging_ev)
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return false;
     cuda_ready = true;
     return true;
 }
 
-void FkvPromo::promote(const Record& r) {
-    Archive& a = archives[r.layer];
-    Blob& bl = blobs[r.layer];
-    if (!a.k || !bl.near_k) return;   // nothing to promote into (reference: :215-216)
-    const int idx = r.b * bl.H + r.h;
-    const int32_t cur = bl.shadow[idx];
-    if (cur >= bl.Np) {
-        headroom_full.fetch_add(1);
-        return;
-    }
-    const size_t row = (size_t)a.D * sizeof(uint16_t);
-    if (!ensure_cuda(2 * row + 16)) {
+void FkvPromo::promote_batch(std::vector<Record>& batch) {
+    if (!ensure_cuda()) {
         worker_error = "promotion worker: CUDA setup failed";
         return;
     }
-    const int slot = next_slot;
-    next_slot = (next_slot + 1) % kStagingSlots;
-    cudaEventSynchronize(slot_ev[slot]);   // previous copies out of this slot are done
-    uint8_t* st = staging + (size_t)slot * slot_bytes;
-    const size_t src = ((size_t)(r.b * a.H + r.h) * a.S + r.arc_local) * a.D;
-    std::memcpy(st, a.k + src, row);
-    std::memcpy(st + row, a.v + src, row);
-    int32_t* cnt = reinterpret_cast<int32_t*>(st + 2 * row);
-    *cnt = cur + 1;
-    const size_t dst = ((size_t)idx * bl.Np + cur) * bl.D;
-    cudaMemcpyAsync(bl.near_k + dst, st, row, cudaMemcpyHostToDevice, stream);
-    cudaMemcpyAsync(bl.near_v + dst, st + row, row, cudaMemcpyHostToDevice, stream);
-    cudaMemcpyAsync(bl.near_valid + idx, cnt, sizeof(int32_t), cudaMemcpyHostToDevice, stream);
-    cudaEventRecord(slot_ev[slot], stream);
-    bl.shadow[idx] = cur + 1;
-    completed.fetch_add(1);
+    // records of one layer share a near tier and an archive: one batch each
+    std::stable_sort(batch.begin(), batch.end(),
+                     [](const Record& a, const Record& b) { return a.layer < b.layer; });
+    size_t i = 0;
+    while (i < batch.size()) {
+        size_t j = i;
+        while (j < batch.size() && batch[j].layer == batch[i].layer) ++j;
+        promote_layer(batch[i].layer, batch.data() + i, j - i);
+        i = j;
+    }
+}
+
+void FkvPromo::promote_layer(int layer, const Record* recs, size_t n) {
+    Archive& a = archives[layer];
+    Blob& bl = blobs[layer];
+    if (!a.k || !bl.near_k) return;   // nothing to promote into (reference: :215-216)
+    const int D = a.D;
+    // destinations from the host shadow of near_valid; full headroom is counted
+    std::vector<const Record*> ok;
+    std::vector<int64_t> dst;
+    std::vector<int32_t> upd;   // (index, new count) of each touched (b, h), in order
+    std::unordered_map<int, size_t> upd_at;
+    ok.reserve(n);
+    dst.reserve(n);
+    for (size_t r = 0; r < n; ++r) {
+        const int idx = recs[r].b * bl.H + recs[r].h;
+        const int32_t cur = bl.shadow[idx];
+        if (cur >= bl.Np) {
+            headroom_full.fetch_add(1);
+            continue;
+        }
+        bl.shadow[idx] = cur + 1;
+        ok.push_back(recs + r);
+        dst.push_back((int64_t)idx * bl.Np + cur);
+        auto it = upd_at.find(idx);
+        if (it == upd_at.end()) {
+            upd_at[idx] = upd.size();
+            upd.push_back(idx);
+            upd.push_back(cur + 1);
+        } else {
+            upd[it->second + 1] = cur + 1;
+        }
+    }
+    const int m = (int)(upd.size() / 2), cnt = (int)ok.size();
+    if (cnt == 0) return;
+    const size_t row = (size_t)D * sizeof(uint16_t);
+    const size_t bytes = 2 * row * cnt + sizeof(int64_t) * cnt + upd.size() * sizeof(int32_t);
+    // pinned buffer: wait until the copy out of its previous batch is done
+    const int bi = next_buf;
+    next_buf = (next_buf + 1) % kStagingBufs;
+    if (cudaEventSynchronize(staging_ev[bi]) != cudaSuccess) {
+        worker_error = "promotion worker: staging event failed";
+        return;
+    }
+    if (bytes > staging_bytes[bi]) {
+        if (staging[bi]) cudaFreeHost(staging[bi]);
+        staging_bytes[bi] = std::max(bytes, 2 * staging_bytes[bi]);
+        if (cudaHostAlloc((void**)&staging[bi], staging_bytes[bi], cudaHostAllocDefault) != cudaSuccess) {
+            staging[bi] = nullptr;
+            staging_bytes[bi] = 0;
+            worker_error = "promotion worker: pinned staging allocation failed";
+            return;
+        }
+    }
+    if (bytes > dev_stage_bytes) {
+        // the previous device buffer may still be read by queued scatters
+        cudaStreamSynchronize(stream);
+        if (dev_stage) cudaFree(dev_stage);
+        dev_stage_bytes = std::max(bytes, 2 * dev_stage_bytes);
+        if (cudaMalloc(&dev_stage, dev_stage_bytes) != cudaSuccess) {
+            dev_stage = nullptr;
+            dev_stage_bytes = 0;
+            worker_error = "promotion worker: device staging allocation failed";
+            return;
+        }
+    }
+    uint8_t* st = staging[bi];
+    uint16_t* sk = reinterpret_cast<uint16_t*>(st);
+    uint16_t* sv = reinterpret_cast<uint16_t*>(st + row * cnt);
+    for (int r = 0; r < cnt; ++r) {
+        const size_t src = ((size_t)(ok[r]->b * a.H + ok[r]->h) * a.S + ok[r]->arc_local) * D;
+        std::memcpy(sk + (size_t)r * D, a.k + src, row);
+        std::memcpy(sv + (size_t)r * D, a.v + src, row);
+    }
+    std::memcpy(st + 2 * row * cnt, dst.data(), sizeof(int64_t) * cnt);
+    std::memcpy(st + 2 * row * cnt + sizeof(int64_t) * cnt, upd.data(), upd.size() * sizeof(int32_t));
+    if (cudaMemcpyAsync(dev_stage, st, bytes, cudaMemcpyHostToDevice, stream) != cudaSuccess ||
+        cudaEventRecord(staging_ev[bi], stream) != cudaSuccess ||
+        fkv::promo_scatter(dev_stage, cnt, m, D, bl.near_k, bl.near_v, bl.near_valid, stream) != FKV_OK) {
+        worker_error = "promotion worker: batch copy / scatter launch failed";
+        return;
+    }
+    completed.fetch_add((uint64_t)cnt);
 }
 
 FkvPromo::~FkvPromo() {
@@ -182,10 +245,12 @@ FkvPromo::~FkvPromo() {
     if (cuda_ready) {
         cudaSetDevice(device);
         cudaStreamSynchronize(stream);
-        for (auto& e : slot_ev) cudaEventDestroy(e);
+        for (auto& e : staging_ev) cudaEventDestroy(e);
         cudaEventDestroy(done);
         cudaStreamDestroy(stream);
-        if (staging) cudaFreeHost(staging);
+        for (auto* b : staging)
+            if (b) cudaFreeHost(b);
+        if (dev_stage) cudaFree(dev_stage);
     }
     for (auto& a : archives) {
         if (a.map_k) munmap(a.map_k, a.map_bytes);

@@ -6,8 +6,11 @@
  * ``stream`` is a cudaStream_t passed as void* (NULL = legacy default stream).
  * Every entry returns 0 on success or a negative FKV_ERR_* code; the message
  * of the last failure on the calling thread is returned by fkv_last_error().
- * No entry point allocates device memory: scratch space ("workspace") is
- * passed in by the caller, sized by the matching *_workspace_bytes() call.
+ * No decode or compress entry point allocates device memory: scratch space
+ * ("workspace") is passed in by the caller, sized by the matching
+ * *_workspace_bytes() call.  The promotion pipeline (fkv_promo_*) owns its
+ * pinned host staging and one device staging buffer, allocated and grown by
+ * its worker thread.
  *
  * Each declaration cites the reference interface it replaces
  * (samfurr/foveated_kv 0.2.0, path within that project).
@@ -194,7 +197,8 @@ int fkv_decode_qk_path(const FkvDecodeShape* s, const uint8_t* far_k);
  * the workspace; >= 2 = the CTAs of a cluster share the stream's stages
  * dynamically and merge through distributed shared memory), out[3] =
  * clusters per (b, kv head, head group).  turbo != 0 for fkv_decode_turbo.
- * FKV_CLUSTER=0 in the environment disables the cluster mode. */
+ * The cluster mode is opt-in: FKV_CLUSTER=1 in the environment enables it
+ * for small jobs (it measured slower than the flat split on B200). */
 int fkv_decode_plan(const FkvDecodeShape* s, const uint8_t* far_k, int32_t turbo, int32_t* out);
 
 /* TurboQuant far tier, scores directly on codes.  Replaces
@@ -273,9 +277,11 @@ int fkv_combine_partials_strided(int32_t P, int32_t N, int32_t D, const float* p
 /* Opaque pipeline handle.  Replaces foveated::PromotionPipeline
  * (csrc/promotion_pipeline.h:75-141, csrc/promotion_pipeline.cpp:20-248) and
  * its binding (csrc/bindings.cpp:42-100).  One worker std::thread per
- * pipeline copies exact fp16 rows from a host archive (mmapped file or pinned
- * memory) into near-tier headroom with cudaMemcpyAsync on its own stream, then
- * stream-orders the bump of near_valid[b,h]. */
+ * pipeline takes every queued promotion at once, packs the exact fp16 rows
+ * from the host archive (mmapped file or pinned memory) into pinned staging,
+ * moves the batch with one cudaMemcpyAsync on its own stream and scatters it
+ * into near-tier headroom with a kernel, then (stream-ordered, in a second
+ * kernel) stores the new near_valid[b,h] counts. */
 typedef struct FkvPromo FkvPromo;
 
 FkvPromo* fkv_promo_create(int32_t n_layers, int32_t cooldown_steps, int32_t max_per_drain,
