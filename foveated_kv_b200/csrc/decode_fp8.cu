@@ -1228,7 +1228,10 @@ __device__ __forceinline__ void cluster_merge(const DecodeParams& p, int s, int 
 // counter in the shared memory of cluster rank 0, so CTAs that run faster
 // take more stages; the CTA records are then merged through distributed
 // shared memory instead of global records and a ticket.
-template <int D, int VG, int NH = 0, bool CL = false>
+// RT: the progress waits take the caller's iteration limit (p.wait_limit) and
+// the test hook p.test_stall is honoured; without RT both are compile-time
+// (the fixed limit, no hook), which keeps the hot loop's registers down.
+template <int D, int VG, int NH = 0, bool CL = false, bool RT = false>
 __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
     decode_fp8_kernel(const DecodeParams p, const __grid_constant__ TMaps maps) {
     using R = RecLayout<D>;
@@ -1237,6 +1240,7 @@ __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
     constexpr bool UM = NH > 0;
     static_assert(!UM || (D == 128 && VG != kTurbo), "tensor-core far path: fp8 K, D = 128");
     static_assert(!(UM && CL), "cluster mode runs on the mma.sync far path");
+    const uint32_t wlim = RT ? p.wait_limit : kWaitLimit;
     extern __shared__ __align__(128) uint8_t smem_raw[];
     // 1024-byte aligned base: the swizzled TMA boxes and UMMA operands
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1394,7 +1398,7 @@ __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
             } else if constexpr (!UM) {
                 for (int k = 0; k < nstage; ++k) {
                     if (k >= kStages &&
-                        !mbar_wait(empty + k % kStages, ((k / kStages) - 1) & 1, p.wait_limit)) {
+                        !mbar_wait(empty + k % kStages, ((k / kStages) - 1) & 1, wlim)) {
                         atomicExch(p.status, FKV_ERR_TIMEOUT);
                         break;
                     }
@@ -1449,7 +1453,7 @@ __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
                     }
                     if (prog) {
                         idle = 0;
-                    } else if (++idle > p.wait_limit) {
+                    } else if (++idle > wlim) {
                         ok = false;
                         break;
                     } else {
@@ -1474,7 +1478,7 @@ __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
                     int k_next = done ? nstage : (int)atom_add_peer(ctr, 1u);
                     while (!done) {
                         const int slot = j % kStages;
-                        if (!mbar_wait(empty + slot, ((j / kStages) - 1) & 1, p.wait_limit)) {
+                        if (!mbar_wait(empty + slot, ((j / kStages) - 1) & 1, wlim)) {
                             atomicExch(p.status, FKV_ERR_TIMEOUT);
                             break;
                         }
@@ -1565,11 +1569,11 @@ __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
     st.init();
     const int64_t srow0 = (int64_t)s * p.F;
     int failed_at = -1;
-    if (p.test_stall) {
+    if (RT && p.test_stall) {
         // test hook: a wait that nothing satisfies, so the timeout path runs
         // (error status, bounded drain of the copies in flight, normal exit)
         // without any fault
-        if (!mbar_wait(reinterpret_cast<uint64_t*>(smem + RG::STALLBAR), 0, p.wait_limit)) {
+        if (!mbar_wait(reinterpret_cast<uint64_t*>(smem + RG::STALLBAR), 0, wlim)) {
             atomicExch(p.status, FKV_ERR_TIMEOUT);
             failed_at = 0;
         }
@@ -1584,7 +1588,7 @@ __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
         if constexpr (!CL) stage_at<D>(sg, k, seg, start, cnt);
         // (outside cluster mode the consumers' data waits keep the fixed
         // limit; the stall test never reaches them)
-        if (!mbar_wait(full + slot, (jj / kStages) & 1, CL ? p.wait_limit : kWaitLimit)) {
+        if (!mbar_wait(full + slot, (jj / kStages) & 1, wlim)) {
             atomicExch(p.status, FKV_ERR_TIMEOUT);
             failed_at = jj;
             break;
@@ -1614,13 +1618,13 @@ __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
                     load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
                     load_sz<D, VG>(sc, ze, u0[1], cnt, lane, sz[1]);
                     ok = far_tiles_um<D, VG, 2, NH>(kbuf, vbuf, u0, cnt, start, lane, w, ta, escale, mmab,
-                                                    par, kWaitLimit, sz, st);
+                                                    par, wlim, sz, st);
                 } else if (32 * w < cnt) {
                     const int u0[1] = {32 * w};
                     uint32_t sz[1][4];
                     load_sz<D, VG>(sc, ze, u0[0], cnt, lane, sz[0]);
                     ok = far_tiles_um<D, VG, 1, NH>(kbuf, vbuf, u0, cnt, start, lane, w, ta, escale, mmab,
-                                                    par, kWaitLimit, sz, st);
+                                                    par, wlim, sz, st);
                 }
             }
             if (!ok) {
@@ -1940,6 +1944,16 @@ KernelPick pick_cl_kernel(const FkvDecodeShape* sh, bool turbo) {
                                 : KernelPick{decode_fp8_kernel<128, 32, 0, true>, Ring<128, 32>::BYTES + 1024};
     return sh->v_group == 0 ? KernelPick{decode_fp8_kernel<64, 0, 0, true>, Ring<64, 0>::BYTES + 1024}
                             : KernelPick{decode_fp8_kernel<64, 32, 0, true>, Ring<64, 32>::BYTES + 1024};
+}
+
+// Kernels that honour a caller wait limit and the stall test hook
+// (FkvDecodeShape.wait_limit / test_flags): fp8 K with per-token INT4 V at
+// D = 128, on both q.K paths.  Returns fn = nullptr for other shapes.
+KernelPick pick_rt_kernel(const FkvDecodeShape* sh, bool turbo, int nh) {
+    if (turbo || sh->D != 128 || sh->v_group != 0) return KernelPick{nullptr, 0};
+    if (nh == 4) return KernelPick{decode_fp8_kernel<128, 0, 4, false, true>, UmLayout<128, 0>::BYTES};
+    if (nh == 8) return KernelPick{decode_fp8_kernel<128, 0, 8, false, true>, UmLayout<128, 0>::BYTES};
+    return KernelPick{decode_fp8_kernel<128, 0, 0, false, true>, Ring<128, 0>::BYTES + 1024};
 }
 
 int resident_for(const FkvDecodeShape* sh, bool turbo, int nh = -1) {
@@ -2274,6 +2288,13 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
         }
     }
     const bool cl = pl.csize >= 2;
+    if (sh->wait_limit != 0 || sh->test_flags != 0) {
+        FKV_REQUIRE(!cl, FKV_ERR_UNSUPPORTED, "wait_limit / test_flags are not honoured in cluster mode");
+        const KernelPick rk = pick_rt_kernel(sh, turbo, nh);
+        FKV_REQUIRE(rk.fn != nullptr, FKV_ERR_UNSUPPORTED,
+                    "wait_limit / test_flags need D = 128 with per-token INT4 V (fp8 far tier)");
+        kp = rk;   // same layout, plan and residency as the kernel it replaces
+    }
     const size_t qoff = (pl.ticket_bytes + 255) & ~(size_t)255;
     const size_t front = turbo && !cl ? qoff + pl.qproj_bytes : pl.ticket_bytes;
     const size_t need = pl.rec_bytes + front + 256;

@@ -133,6 +133,9 @@ typedef struct FkvDecodeShape {
     int32_t num_splits;    /* split-K chunks per (b,h); 0 = automatic */
     float spike_margin;    /* flag = max_far > min_near + spike_margin */
     float qjl_coef;        /* turbo only: QJL term = qjl_coef/D * gamma * <sign, q S^T> */
+    /* wait_limit / test_flags: honoured for fp8 K with per-token INT4 V at
+       D = 128 outside the cluster mode; other shapes return FKV_ERR_UNSUPPORTED
+       when either is set. */
     int32_t wait_limit;    /* iteration limit of the kernel's progress waits; 0 = default
                               (2^26).  On expiry the kernel records FKV_ERR_TIMEOUT in the
                               workspace status word (fkv_decode_status), lets its copies
