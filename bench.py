@@ -464,13 +464,15 @@ def main_seqsplit(args, rank, world, device):
     torch.cuda.synchronize()
     compress_ms = e0.elapsed_time(e1)
     del w
-    # one GPU: the step (partial + combine kernels) is captured in a CUDA
-    # graph; several GPUs: eager steps (the NCCL all-gather is not captured)
-    # prepared per-layer step: one partial call, one all-gather, one strided
-    # combine (buffers allocated once, little host work per step)
-    dec = SeqSplitDecoder(lay, off, Hq)
+    # prepared per-layer step, buffers allocated once: one partial launch and,
+    # with several GPUs, one fused peer-store exchange + merge launch per
+    # rank (FKV_C4_EXCHANGE=nccl: NCCL all-gather + strided merge, eager);
+    # the peer-exchange step and the single-GPU step are captured in a CUDA
+    # graph (the NCCL collective is never captured)
+    exch = os.environ.get("FKV_C4_EXCHANGE", "peer")
+    dec = SeqSplitDecoder(lay, off, Hq, exchange=exch)
     graph = None
-    if world == 1:
+    if world == 1 or dec.peer is not None:
         gs = torch.cuda.Stream(device)
         with torch.cuda.stream(gs):
             for _ in range(max(args.warmup, 3)):
@@ -547,7 +549,10 @@ def main_seqsplit(args, rank, world, device):
                        "near_pct": c["near_pct"],
                        "parallelism": f"sequence split x{world} (equal-cost shards)",
                        "shard": [lo, hi],
-                       "exchange": "NCCL all-gather of (m, l, o) records + combine kernel",
+                       "exchange": ("peer-store exchange + merge in one launch per rank "
+                                    "(CUDA IPC over NVLink), step captured in a CUDA graph"
+                                    if dec.peer is not None else
+                                    "NCCL all-gather of (m, l, o) records + combine kernel"),
                        "qk_path": qk_path_name(lay, Hq)},
             "us_per_layer": ms * 1e3, "compress_ms": compress_ms,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

@@ -83,6 +83,13 @@ SIGNATURES = {
     "fkv_combine_partials": (C.c_int, [I32, I32, I32, P, P, C.c_float, P, P, P, P]),
     "fkv_combine_partials_strided": (C.c_int, [I32, I32, I32, P, C.c_int64, P, C.c_int64, C.c_float,
                                                P, P, P, P]),
+    "fkv_exchange_recv_bytes": (SZ, [I32, I32, I32]),
+    "fkv_exchange_block_stride": (I64, [I32, I32]),
+    "fkv_exchange_combine": (C.c_int, [I32, I32, I32, I32, P, P, P, P, C.c_float, P, P, P, P]),
+    "fkv_ipc_handle_bytes": (C.c_int, []),
+    "fkv_ipc_get_handle": (C.c_int, [P, P, C.POINTER(I64)]),
+    "fkv_ipc_open": (C.c_int, [P, I64, C.POINTER(P)]),
+    "fkv_ipc_close": (C.c_int, [P, I64]),
     "fkv_promo_create": (P, [I32, I32, I32, I32]),
     "fkv_promo_register_archive": (C.c_int, [P, I32, C.c_char_p, C.c_char_p, I32, I32, I32,
                                              I32, P, I64]),

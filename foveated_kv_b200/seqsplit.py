@@ -212,7 +212,10 @@ class SeqSplitDecoder:
     several ranks share a host's cores.  The tensors step() returns are
     overwritten by the next step: copy them to keep them."""
 
-    def __init__(self, layer: FoveatedLayer, far_offset: int, Hq: int, group=None):
+    def __init__(self, layer: FoveatedLayer, far_offset: int, Hq: int, group=None,
+                 exchange: str = "nccl"):
+        """exchange: 'nccl' (all-gather + strided merge) or 'peer' (one
+        fused peer-store exchange + merge launch, PeerExchange)."""
         self.lib = _native.load()
         self.layer, self.far_offset, self.group = layer, int(far_offset), group
         self.P = dist.get_world_size(group) if (dist.is_available() and dist.is_initialized()) else 1
@@ -223,9 +226,15 @@ class SeqSplitDecoder:
         self.sh = _native.DecodeShape()
         self.ws = None
         self._refresh_shape()
-        self.flat = torch.empty((self.rec,), dtype=torch.float32, device=dev)
-        self.gathered = (torch.empty((self.P * self.rec,), dtype=torch.float32, device=dev)
-                         if self.P > 1 else self.flat)
+        self.peer = None
+        if exchange == "peer" and self.P > 1:
+            self.peer = PeerExchange(self.N, self.D, dev, group)
+            self.flat = torch.zeros((self.peer.stride,), dtype=torch.float32, device=dev)
+            self.gathered = self.flat
+        else:
+            self.flat = torch.empty((self.rec,), dtype=torch.float32, device=dev)
+            self.gathered = (torch.empty((self.P * self.rec,), dtype=torch.float32, device=dev)
+                             if self.P > 1 else self.flat)
         self.qbuf = torch.empty((self.B, Hq, self.D), dtype=F16, device=dev)
         self.out = torch.empty((self.N, self.D), dtype=F16, device=dev)
         self.flags = torch.empty((self.N,), dtype=I32, device=dev)
@@ -259,6 +268,10 @@ class SeqSplitDecoder:
             _p(lay.far_v), _p(lay.far_v_scale), _p(lay.far_v_zero), _p(qq), _p(dk), _p(dv),
             self.far_offset, base, base + N * (D + 4) * 4, self.ws.data_ptr(), self.ws.numel(), st),
             "fkv_decode_fp8_partial")
+        if self.peer is not None:
+            self.peer.combine(self.flat, lay.spike_margin, self.out, self.flags, self.tokens)
+            return (self.out.view(self.B, self.Hq, 1, D), self.flags.view(self.B, self.Hq),
+                    self.tokens.view(self.B, self.Hq))
         if self.P > 1:
             dist.all_gather_into_tensor(self.gathered, self.flat, group=self.group)
         g = self.gathered.data_ptr()
@@ -268,3 +281,61 @@ class SeqSplitDecoder:
             "fkv_combine_partials_strided")
         return (self.out.view(self.B, self.Hq, 1, D), self.flags.view(self.B, self.Hq),
                 self.tokens.view(self.B, self.Hq))
+
+
+class PeerExchange:
+    """Receive buffers of a sequence split mapped into every rank (CUDA IPC
+    over NVLink), for fkv_exchange_combine: one launch per rank that writes
+    its record block into every peer's buffer with plain peer stores and
+    merges once all P blocks of the step have arrived (bounded wait).  No
+    NCCL call on the step's path, so the whole step can be captured in a
+    CUDA graph.  One rank per GPU; the handles are exchanged once through the
+    process group."""
+
+    def __init__(self, N: int, D: int, device, group=None):
+        self.lib = lib = _native.load()
+        self.P = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.N, self.D = N, D
+        self.stride = int(lib.fkv_exchange_block_stride(N, D))
+        nbytes = int(lib.fkv_exchange_recv_bytes(self.P, N, D))
+        self.recv = torch.zeros((nbytes // 4 + 16,), dtype=torch.float32, device=device)
+        base = self.recv.data_ptr()
+        self.recv_ptr = (base + 63) & ~63
+        self.state = torch.zeros((4,), dtype=I32, device=device)
+        hb = lib.fkv_ipc_handle_bytes()
+        handle = (C.c_uint8 * hb)()
+        off = C.c_int64(0)
+        _native.check(lib.fkv_ipc_get_handle(self.recv_ptr, handle, C.byref(off)), "fkv_ipc_get_handle")
+        mine = (bytes(handle), int(off.value))
+        allh = [None] * self.P
+        dist.all_gather_object(allh, mine, group=group)
+        self.opened = []
+        ptrs = []
+        for r, (h, o) in enumerate(allh):
+            if r == self.rank:
+                ptrs.append(self.recv_ptr)
+                continue
+            out = C.c_void_p()
+            hbuf = (C.c_uint8 * hb).from_buffer_copy(h)
+            _native.check(lib.fkv_ipc_open(hbuf, o, C.byref(out)), "fkv_ipc_open")
+            self.opened.append((out.value, o))
+            ptrs.append(out.value)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)       # every rank's buffers are mapped before any step
+
+    def combine(self, local_block: torch.Tensor, margin: float, out, flags, tokens):
+        _native.check(self.lib.fkv_exchange_combine(
+            self.P, self.rank, self.N, self.D, local_block.data_ptr(), self.peers.data_ptr(),
+            self.recv_ptr, self.state.data_ptr(), float(margin), out.data_ptr(), flags.data_ptr(),
+            tokens.data_ptr(), _stream(local_block.device)), "fkv_exchange_combine")
+
+    def status(self) -> int:
+        """FKV_ERR_TIMEOUT (-4) if a peer's block did not arrive in some step."""
+        return int(self.state[3].item())
+
+    def close(self):
+        for ptr, off in self.opened:
+            self.lib.fkv_ipc_close(ptr, off)
+        self.opened = []

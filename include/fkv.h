@@ -273,6 +273,39 @@ int fkv_combine_partials_strided(int32_t P, int32_t N, int32_t D, const float* p
                                  int64_t arg_rank_stride, float spike_margin, uint16_t* out,
                                  int32_t* flags, int32_t* tokens, void* stream);
 
+/* Sequence-split exchange over peer memory (no counterpart in the reference,
+ * which has no multi-device code).  Replaces the all-gather + merge of a
+ * sequence-split step with one launch per rank that stores this rank's
+ * [records | argmax] block (fkv_decode_fp8_partial's layout, padded to
+ * fkv_exchange_block_stride floats, 16-byte aligned) into slot `rank` of
+ * every rank's receive buffer with plain peer stores, publishes a sequence
+ * number in every rank's flag for it, waits (bounded) for all P flags of its
+ * own buffer and merges row n of the P blocks in rank order, exactly as
+ * fkv_combine_partials.
+ *   peer_recv  device array of P receive-buffer addresses (own included),
+ *              each fkv_exchange_recv_bytes long, zero-filled once, 64-byte
+ *              aligned; peers' buffers mapped with fkv_ipc_open
+ *   state      4 int32 of this rank, zero-filled once: sequence number, two
+ *              block counters, status (FKV_ERR_TIMEOUT if a peer's block did
+ *              not arrive in about half a second)
+ * Every rank must issue the same sequence of calls; one rank per GPU.
+ * The receive buffers alternate between two halves by step parity. */
+size_t fkv_exchange_recv_bytes(int32_t P, int32_t N, int32_t D);
+int64_t fkv_exchange_block_stride(int32_t N, int32_t D);
+int fkv_exchange_combine(int32_t P, int32_t rank, int32_t N, int32_t D, const float* local_block,
+                         const uint64_t* peer_recv, void* my_recv, int32_t* state,
+                         float spike_margin, uint16_t* out, int32_t* flags, int32_t* tokens,
+                         void* stream);
+
+/* CUDA IPC of a device buffer (no counterpart in the reference): the
+ * handle (fkv_ipc_handle_bytes bytes) names the allocation holding dev_ptr,
+ * and *offset is dev_ptr's offset in it; fkv_ipc_open maps it in another
+ * process (peer access over NVLink) and returns the same offset into it. */
+int fkv_ipc_handle_bytes(void);
+int fkv_ipc_get_handle(const void* dev_ptr, uint8_t* handle, int64_t* offset);
+int fkv_ipc_open(const uint8_t* handle, int64_t offset, void** dev_ptr);
+int fkv_ipc_close(void* dev_ptr, int64_t offset);
+
 /* ------------------------------------------------------------------------ */
 /* Spike drain + promotion                                                  */
 /* ------------------------------------------------------------------------ */

@@ -31,6 +31,27 @@ def main():
     o2, f2, t2 = dec.step(t["q"])          # second step re-uses every buffer
     torch.cuda.synchronize()
     assert torch.equal(o2, out) and torch.equal(f2, fl) and torch.equal(t2, tk)
+    # peer-store exchange (one fused launch per rank, no NCCL on the step),
+    # eager and captured in a CUDA graph, several steps in a row
+    pdec = SeqSplitDecoder(lay, off, Hq, exchange="peer")
+    for _ in range(3):
+        o3, f3, t3 = pdec.step(t["q"])
+        torch.cuda.synchronize()
+        assert torch.equal(o3, out) and torch.equal(f3, fl) and torch.equal(t3, tk)
+    gs = torch.cuda.Stream(dev)
+    gs.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=gs):
+        pdec.step(t["q"])
+    for _ in range(4):
+        pdec.out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(pdec.out.view_as(out), out)
+        assert torch.equal(pdec.flags.view_as(fl), fl) and torch.equal(pdec.tokens.view_as(tk), tk)
+    assert pdec.peer.status() == 0
+    dist.barrier()
+    pdec.peer.close()
     if rank == 0:
         full = compress_layer(t["k"], t["v"], cfg)
         ro, rf, rt = full.attend_fused_with_spikes(t["q"])
