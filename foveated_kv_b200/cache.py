@@ -185,6 +185,9 @@ class FoveatedLayer:
         reference ignores this argument and always uses 10.0).
         """
         lib = _native.load()
+        if not (query.is_cuda and self.near_k.is_cuda) or query.device != self.near_k.device:
+            raise ValueError("attend_fused_with_spikes: query and tiers must be CUDA tensors "
+                             "on the same device")
         B, Hq, D = query.shape[0], query.shape[1], query.shape[-1]
         q = query.reshape(B, Hq, D)
         if q.dtype != F16 or not q.is_contiguous():
@@ -247,29 +250,25 @@ class FoveatedLayer:
     def detect_spikes(self, query: torch.Tensor, margin: float = 0.5) -> Optional[torch.Tensor]:
         """GQA-mean query spike check (``detect_spikes``, mlx_foveated.py:451-490).
 
-        q = mean of the group's query heads; a far token spikes when its
-        score exceeds the lowest near / decode score + margin.  Returns an
-        int32 (N, 3) tensor of [b, kv head, far-local argmax] for the heads
-        with any spike, or None.  An auxiliary policy outside the fused
-        kernel: plain torch ops on the layer's tensors.
+        q = mean of each group's query heads (rounded to fp16, the query
+        dtype); a (b, kv head) spikes when some far score exceeds its lowest
+        near / decode score + margin, and reports its far-local argmax
+        (earliest on ties).  Runs as ONE fused decode launch with the mean
+        queries as one query head per KV head: the kernel's spike emission is
+        exactly this test (its attention output is discarded).  Returns an
+        int32 (N, 3) tensor of [b, kv head, far-local argmax], or None.
         """
         if self.compress_method != "fp8" or self.n_far == 0:
             return None
-        D = query.shape[-1]
-        q = query.reshape(query.shape[0], query.shape[1], D).float()
+        B, D = query.shape[0], query.shape[-1]
+        q = query.reshape(B, query.shape[1], D).float()
         G = q.shape[1] // self.H_kv
-        q = q.reshape(q.shape[0], self.H_kv, G, D).mean(2)                   # (B, H, D)
-        near = self.effective_near_k.float()
-        near_s = torch.einsum("bhd,bhtd->bht", q, near) / math.sqrt(D)
-        thr = near_s.min(dim=-1, keepdim=True).values + margin
-        far = self.far_k.view(torch.float8_e4m3fn).to(torch.float16).float()
-        far_s = torch.einsum("bhd,bhtd->bht", q, far) / math.sqrt(D)
-        mask = (far_s > thr).any(dim=-1)
-        if not bool(mask.any()):
+        qm = q.reshape(B, self.H_kv, G, D).mean(2).to(F16).contiguous()       # (B, H, D)
+        _, flags, tokens = self.attend_fused_with_spikes(qm, spike_margin=margin)
+        bh = flags.nonzero()
+        if bh.numel() == 0:
             return None
-        bh = mask.nonzero()
-        best = far_s.argmax(dim=-1)[bh[:, 0], bh[:, 1]]
-        return torch.stack([bh[:, 0], bh[:, 1], best], 1).to(torch.int32)
+        return torch.cat([bh, tokens[bh[:, 0], bh[:, 1]][:, None]], 1).to(torch.int32)
 
     # ---- promotion target (foveated_attn.cpp:242-254) ---------------------------
     def get_blob_info(self) -> dict:

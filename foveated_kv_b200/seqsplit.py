@@ -119,6 +119,8 @@ def decode_partial(layer: FoveatedLayer, q: torch.Tensor, far_offset: int):
     Both are views of one flat f32 buffer (arg bit-cast), so a single
     collective can exchange them."""
     lib = _native.load()
+    if not (q.is_cuda and layer.near_k.is_cuda):
+        raise ValueError("decode_partial: query and tiers must be CUDA tensors")
     B, Hq, D = q.shape[0], q.shape[1], q.shape[-1]
     qq = q.reshape(B, Hq, D).to(F16).contiguous()
     sh = layer._fill_shape(Hq, layer.spike_margin)

@@ -23,25 +23,42 @@ def _cpu_layer(w, cfg):
                               far_v_zero=t(lay["far_v_zero"]))
 
 
-def test_detect_spikes_matches_reference_semantics():
-    w = numpy_workload(3, 2, 2, 8, 400, 64, 0)
+@pytest.mark.gpu
+@pytest.mark.parametrize("margin", [-100.0, 0.5, 2.0, 1e6])
+def test_detect_spikes_matches_reference_semantics(margin):
+    """detect_spikes runs as one fused launch with the GQA-mean query; it
+    equals a restatement of mlx_foveated.py:451-490 (near + decode scores,
+    far E4M3 scores, 1/sqrt(D)) on the same tiers."""
+    from foveated_kv_b200 import compress_layer
+    w = numpy_workload(3, 2, 2, 8, 1400, 128, 3)
+    t = {k: torch.from_numpy(v).cuda() for k, v in w.items()}
+    lay = compress_layer(t["k"], t["v"], TierConfig(near_pct=0.1, window_size=16))
+    for j in range(3):
+        lay.add_token(t["dec_k"][:, :, j:j + 1], t["dec_v"][:, :, j:j + 1])
+    got = lay.detect_spikes(t["q"], margin)
+    q = w["q"].astype(np.float32).reshape(2, 2, 4, 128).mean(2).astype(np.float16).astype(np.float64)
+    rows, near_v = [], lay.near_valid.cpu().numpy()
+    nk, fk = lay.near_k.cpu().numpy(), lay.far_k.cpu().numpy()
+    for b in range(2):
+        for h in range(2):
+            keys = np.concatenate([nk[b, h, :near_v[b, h]], w["dec_k"][b, h]]).astype(np.float64)
+            ns = keys @ q[b, h] / math.sqrt(128)
+            fs = O.e4m3_to_fp16(fk[b, h]).astype(np.float64) @ q[b, h] / math.sqrt(128)
+            gap = fs.max() - (ns.min() + margin)
+            assert abs(gap) > 1e-3, "seeded case sits on the decision"
+            if gap > 0:
+                rows.append([b, h, int(np.argmax(fs))])
+    if not rows:
+        assert got is None
+    else:
+        assert np.array_equal(got.cpu().numpy(), np.array(rows, dtype=np.int32))
+
+
+def test_fused_calls_reject_host_tensors():
+    w = numpy_workload(3, 1, 2, 8, 400, 64, 0)
     lay, fl = _cpu_layer(w, dict(near_pct=0.1, window_size=16))
-    for margin in (-100.0, 0.5, 1e6):
-        got = fl.detect_spikes(torch.from_numpy(w["q"]), margin)
-        # restatement of mlx_foveated.py:451-490 in fp32
-        q = w["q"].astype(np.float32).reshape(2, 2, 4, 64).mean(2)
-        rows = []
-        for b in range(2):
-            for h in range(2):
-                nv = lay["near_valid"][b, h]
-                ns = lay["near_k"][b, h, :nv].astype(np.float32) @ q[b, h] / math.sqrt(64)
-                fs = O.e4m3_to_fp16(lay["far_k"][b, h]).astype(np.float32) @ q[b, h] / math.sqrt(64)
-                if np.any(fs > ns.min() + margin):
-                    rows.append([b, h, int(np.argmax(fs))])
-        if not rows:
-            assert got is None
-        else:
-            assert np.array_equal(got.numpy(), np.array(rows, dtype=np.int32))
+    with pytest.raises(ValueError, match="CUDA"):
+        fl.attend_fused_with_spikes(torch.from_numpy(w["q"]))
 
 
 def test_archive_rescoring(tmp_path):
