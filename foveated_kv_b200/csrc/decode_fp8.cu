@@ -1819,7 +1819,10 @@ __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
 }
 
 // shard k's record n at parts + k * prs + n * (D + 4), its argmax at
-// args + k * ars + n (prs / ars: element strides between the shards' blocks)
+// args + k * ars + n (prs / ars: element strides between the shards' blocks).
+// With a gathered [records | argmax] layout the stride N * (D + 4) + N is
+// usually not a multiple of 4 floats, so a record may be only 4-byte
+// aligned: this kernel reads the records with scalar loads only.
 template <int D>
 __global__ void combine_kernel(int P, int N, const float* __restrict__ parts, int64_t prs,
                                const int32_t* __restrict__ args, int64_t ars, float margin,
