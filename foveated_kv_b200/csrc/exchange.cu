@@ -40,7 +40,7 @@ using namespace fkvdev;
 namespace {
 
 constexpr int kExThreads = 128;
-constexpr uint32_t kExSpinLimit = 1u << 22;   // x ~100 ns back-off: about half a second
+constexpr uint32_t kExSpinLimit = 1u << 23;   // x 32+ ns back-off: about half a second
 
 __device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
     asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(kExThreads)
                 atomicExch(state + 3, FKV_ERR_TIMEOUT);
                 break;
             }
-            __nanosleep(100);
+            __nanosleep(32);
         }
     }
     __syncthreads();
