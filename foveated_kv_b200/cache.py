@@ -114,6 +114,7 @@ class FoveatedLayer:
         self._dec_v = torch.zeros_like(self._dec_k)
         self._n_dec = 0
         self._shape = _native.DecodeShape()
+        self._nv_snapshot = None
         self._next_pos = int(max(int(near_idx.max().item()) if near_idx.numel() else -1,
                                  int(far_idx.max().item()) if far_idx.numel() else -1)) + 1
 
@@ -206,10 +207,17 @@ class FoveatedLayer:
         dk = self._dec_k if self._n_dec else None
         dv = self._dec_v if self._n_dec else None
         st = _stream(self.device)
+        nv = self.near_valid
+        if self._nv_snapshot is not None:
+            # a promotion worker may bump near_valid while this launch runs:
+            # every CTA of the launch must see one count per stream, so the
+            # launch reads a snapshot taken in stream order just before it
+            self._nv_snapshot.copy_(self.near_valid)
+            nv = self._nv_snapshot
         if self.compress_method == "turbo":
             tc = self._turbo_constants
             rc = lib.fkv_decode_turbo(
-                C.byref(sh), _p(self.near_k), _p(self.near_v), _p(self.near_valid),
+                C.byref(sh), _p(self.near_k), _p(self.near_v), _p(nv),
                 _p(self.turbo_far_k_indices), _p(self.turbo_far_k_signs),
                 _p(self.turbo_far_k_norm), _p(self.turbo_far_k_gamma),
                 _p(self.turbo_far_v_packed), _p(self.turbo_far_v_scale), _p(tc.Pi), _p(tc.S),
@@ -218,7 +226,7 @@ class FoveatedLayer:
             _native.check(rc, "fkv_decode_turbo")
         else:
             rc = lib.fkv_decode_fp8(
-                C.byref(sh), _p(self.near_k), _p(self.near_v), _p(self.near_valid),
+                C.byref(sh), _p(self.near_k), _p(self.near_v), _p(nv),
                 _p(self.far_k), _p(self.far_v), _p(self.far_v_scale), _p(self.far_v_zero), _p(q),
                 _p(dk), _p(dv), _p(out), _p(flags), _p(tokens), ws.data_ptr(), ws.numel(), st)
             _native.check(rc, "fkv_decode_fp8")
@@ -272,6 +280,13 @@ class FoveatedLayer:
 
     # ---- promotion target (foveated_attn.cpp:242-254) ---------------------------
     def get_blob_info(self) -> dict:
+        """Promotion target (the worker writes near_k / near_v rows and
+        near_valid).  From here on the fused decode reads a per-launch
+        snapshot of near_valid, so promotions landing during a launch cannot
+        give its CTAs different counts (the reference's kernel reads
+        near_valid once per dispatch)."""
+        if self._nv_snapshot is None:
+            self._nv_snapshot = torch.empty_like(self.near_valid)
         return {"near_k": self.near_k, "near_v": self.near_v, "near_valid": self.near_valid,
                 "N_near_alloc": self.n_near_alloc, "B": self.B, "H_kv": self.H_kv, "D": self.D}
 

@@ -162,7 +162,10 @@ size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s);
  * spike flags / tokens.  Replaces FoveatedHandle::operator()
  * (csrc/foveated_attn.cpp:164-240) and kernel foveated_2tier
  * (csrc/kernels/foveated_attn.metal:181-432).
- *   near_k/near_v (B,Hk,Np,D) fp16; near_valid (B,Hk) int32
+ *   near_k/near_v (B,Hk,Np,D) fp16; near_valid (B,Hk) int32, read by every
+ *   CTA of the launch: it must not change while the launch runs (when a
+ *   promotion worker may bump it concurrently, pass a copy taken in stream
+ *   order just before the call, as FoveatedLayer does once registered)
  *   far_k (B,Hk,F,D) u8; far_v (B,Hk,F,D/2) u8; v_scale/v_zero as compress
  *   q (B,Hq,D) fp16; dec_k/dec_v (B,Hk,dec_stride,D) fp16 (NULL if n_dec==0)
  *   out (B,Hq,D) fp16, 16-byte aligned; flags (B,Hq) int32; tokens (B,Hq)
