@@ -145,3 +145,31 @@ def test_large_batched_promotion_matches_archive():
         total += len(toks)
     assert pipe.get_stats()["promotions_completed"] == total
     pipe.close()
+
+
+def test_async_promotion_then_parity():
+    """Promotions left to the worker between steps (no flush: the
+    reference's default asynchronous mode) overlap the next decodes; every
+    launch reads a snapshot of near_valid, and after a final flush the tiers
+    and the decode agree with the oracle."""
+    w, t, lay = _setup(B=2, Hk=2, Hq=8, S=1500)
+    pipe = PromotionPipeline(1, cooldown_steps=0, max_per_drain=64)
+    pipe.register_archive_host(0, lay.archive_k.cpu().pin_memory(), lay.archive_v.cpu().pin_memory(),
+                               lay.far_idx)
+    pipe.register_blob(0, lay.get_blob_info())
+    R0 = np_(lay.near_valid).copy()
+    rng = np.random.default_rng(1)
+    for step in range(6):
+        out, fl, tk = lay.attend_fused_with_spikes(t["q"])
+        toks = rng.integers(0, lay.n_far, (2, 8)).astype(np.int32)
+        pipe.drain_spikes(0, np.ones((2, 8), np.int32), toks, lay.far_idx, step)
+        assert torch.isfinite(out.float()).all()
+    pipe.flush()
+    torch.cuda.synchronize()
+    nv = np_(lay.near_valid)
+    assert int((nv - R0).sum()) == pipe.get_stats()["promotions_completed"] > 0
+    out, fl, tk = lay.attend_fused_with_spikes(t["q"])
+    torch.cuda.synchronize()
+    rout, rfl, rtk, diag = O.decode_attend(layer_to_oracle(lay), w["q"], None, None, 0.5)
+    assert_output_close(np_(out).astype(np.float64)[:, :, 0], rout, "after async promotion")
+    pipe.close()
