@@ -111,7 +111,7 @@ def algorithmic_bytes(B, Hq, Hk, D, near_valid_sum, F, n_dec, turbo=False):
             + B * Hq * D * (2 + 2) + B * Hq * 8)
 
 
-def build_layer(cfgname, seed, device, batch=0):
+def build_layer(cfgname, seed, device, batch=0, time_compress=False):
     import torch
     from foveated_kv_b200 import TierConfig, compress_layer
     from foveated_kv_b200.synthetic import torch_workload, inject_spikes_torch, CONFIGS
@@ -126,13 +126,20 @@ def build_layer(cfgname, seed, device, batch=0):
         inject_spikes_torch(w, cfg.tier_boundaries(c["S"]), seed)
     # importance selection (c0) scores tokens with the seeded query
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    e0.record()
-    lay = compress_layer(w["k"], w["v"], cfg,
-                         query=w["q"] if c["select"] == "importance" else None)
-    e1.record()
-    torch.cuda.synchronize()
-    lay.compress_ms = e0.elapsed_time(e1)
+    qo = w["q"] if c["select"] == "importance" else None
+    lay = compress_layer(w["k"], w["v"], cfg, query=qo)
+    if time_compress:
+        # time a second pass with the allocator's blocks already cached (the
+        # first pass of a shape includes cudaMalloc of its output tiers)
+        del lay
+        torch.cuda.synchronize()
+        e0.record()
+        lay = compress_layer(w["k"], w["v"], cfg, query=qo)
+        e1.record()
+        torch.cuda.synchronize()
+        lay.compress_ms = e0.elapsed_time(e1)
+    else:
+        lay.compress_ms = None
     for i in range(c["n_dec"]):
         lay.add_token(w["dec_k"][:, :, i:i + 1], w["dec_v"][:, :, i:i + 1])
     q = w["q"]
@@ -390,10 +397,19 @@ def promotion_step_bench(cfgname, device, steps, warmup, budget, batch=0, rounds
     arc_v = lay.archive_v.cpu().pin_memory()
     lay.archive_k = lay.archive_v = None
     torch.cuda.empty_cache()
-    pipe = PromotionPipeline(1, cooldown_steps=5, max_per_drain=budget)
-    pipe.register_archive_host(0, arc_k, arc_v, lay.far_idx)
-    pipe.register_blob(0, lay.get_blob_info())
-    nv0 = int(lay.near_valid.sum().item())
+    nv_init = lay.near_valid.clone()
+    nv0 = int(nv_init.sum().item())
+
+    def fresh_pipeline():
+        # each mode starts from the compressed tiers: empty headroom, no
+        # promotion history (position dedup would otherwise block the pool)
+        lay.near_valid.copy_(nv_init)
+        torch.cuda.synchronize()
+        p_ = PromotionPipeline(1, cooldown_steps=5, max_per_drain=budget)
+        p_.register_archive_host(0, arc_k, arc_v, lay.far_idx)
+        p_.register_blob(0, lay.get_blob_info())
+        return p_
+    pipe = None
     fl_h = torch.empty((B, Hq), dtype=torch.int32).pin_memory()
     tk_h = torch.empty((B, Hq), dtype=torch.int32).pin_memory()
     st = torch.cuda.current_stream()
@@ -418,6 +434,9 @@ def promotion_step_bench(cfgname, device, steps, warmup, budget, batch=0, rounds
     t_next = 0
     for m in modes:
         mode["flush"] = m == "flush"
+        if pipe is not None:
+            pipe.close()
+        pipe = fresh_pipeline()
         for _ in range(max(warmup, 3)):
             step(t_next)
             t_next += 1
@@ -441,14 +460,14 @@ def promotion_step_bench(cfgname, device, steps, warmup, budget, batch=0, rounds
         done = after["promotions_completed"] - before["promotions_completed"]
         assert nv_after - nv_before == done, (nv_after - nv_before, done)
         res[m] = {"ms_per_step": ms, "promotions_per_step": done / steps,
-                  "queued_per_step_max": max(queued)}
+                  "queued_per_step_max": max(queued),
+                  "rows_promoted": int(lay.near_valid.sum().item()) - nv0}
     lay.check_decode()
     after = pipe.get_stats()
     pipe.close()
     out = dict(res.get("flush", {}))
     out.update({"modes": res, "budget_per_drain": budget, "cooldown_steps": 5,
                 "spikes_per_stream_per_step": n,
-                "rows_promoted_total": int(lay.near_valid.sum().item()) - nv0,
                 "headroom_full": after["promotions_headroom_full"],
                 "what": "per step: re-inject 1% spikes, fused decode, D2H flags/tokens, drain "
                         "(PromotionPipeline), batched H2D of exact fp16 rows + scatter kernel; "
@@ -607,7 +626,7 @@ def main():
     if args.config == "c4":
         return main_seqsplit(args, rank, world, device)
 
-    c, cfg, lay, q = build_layer(args.config, 1000 + rank, device, args.batch)
+    c, cfg, lay, q = build_layer(args.config, 1000 + rank, device, args.batch, time_compress=True)
     B, Hq, Hk, D = c["B"], c["Hq"], c["Hk"], c["D"]
     tier_bytes = lay.memory_bytes()["total_quantized"]
     # distinct layers so that one graph replay streams >= ~4 GB (no L2 reuse
@@ -693,8 +712,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(args.config, args.cpu_sample_seqs)
-    # first compress of the process pays one-off set-up; later layers are steady state
-    compress_ms = statistics.median(L_.compress_ms for L_ in (layers[1:] or layers))
+    compress_ms = layers[0].compress_ms
     del layers, outs, graph
     torch.cuda.empty_cache()
     promo = None
