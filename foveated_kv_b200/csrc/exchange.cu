@@ -3,25 +3,27 @@
 // Each rank of a sequence split holds one block of partial records
 // ([N records of (m, l, min_near, max_far, o[D])] followed by N argmax
 // values) after its partial decode.  fkv_exchange_combine replaces the
-// all-gather + merge of that step with ONE kernel launch per rank:
+// all-gather + merge of that step with ONE kernel launch per rank.  Block n
+// handles output row n:
 //
-//   1. every block copies its share of the local record block into slot
-//      `rank` of every rank's receive buffer with plain stores to the peers'
-//      memory (CUDA IPC mappings over NVLink; no TMA, no multicast);
-//   2. the block that finishes the copies last (a counter in the rank's own
-//      state words) publishes the step's sequence number in every rank's
-//      flag for this rank (release, system scope);
-//   3. every block waits (bounded, acquire) until all P flags of its own
-//      receive buffer carry the step's sequence number, then merges the P
-//      records of its output row n in rank order (earliest rank wins max_far
+//   1. it sends row n of the local block (D + 4 record words and the argmax)
+//      to slot `rank` of every rank's receive buffer, each 4-byte word paired
+//      with the step's sequence number in one 8-byte store (plain stores to
+//      the peers' memory through CUDA IPC mappings over NVLink; no TMA, no
+//      multicast).  A word and its tag land together, so no fence or flag is
+//      needed (the low-latency protocol NCCL calls LL);
+//   2. it polls (bounded) its own receive buffer until row n of all P ranks
+//      carries the step's tag, staging the values in shared memory;
+//   3. it merges the P records in rank order (earliest rank wins max_far
 //      ties), as fkv_combine_partials does.
 //
 // Receive buffers are double-buffered by the parity of the sequence number:
-// a rank can only start writing step t + 2 into a peer after its own step
-// t + 1 merge, which waited for the peer's step t + 1 flag, which the peer
-// wrote after finishing its step t merge -- so no slot is overwritten while
-// it is read.  The sequence number lives in device memory (state[0]) and is
-// advanced by the launch itself, so a captured step replays correctly.
+// a rank can only write step t + 2 into a peer after its own step t + 1
+// merge, which needed the peer's step t + 1 rows, which the peer sent after
+// finishing its step t merge -- so no slot is overwritten while it is read,
+// and a stale word (tag t) never passes for a fresh one (tag t + 2).  The
+// sequence number lives in device memory (state[0]) and is advanced by the
+// launch itself, so a captured step replays correctly.
 //
 // No counterpart in the reference (it has no multi-device code).
 #include <cuda.h>
@@ -40,82 +42,78 @@ using namespace fkvdev;
 namespace {
 
 constexpr int kExThreads = 128;
-constexpr uint32_t kExSpinLimit = 1u << 23;   // x 32+ ns back-off: about half a second
+constexpr int kExMaxRanks = 8;
+constexpr uint32_t kExSpinLimit = 1u << 22;   // polls of one word, ~0.1 us each: under a second
 
-__device__ __forceinline__ void st_release_sys(int32_t* p, int32_t v) {
-    asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
 }
-__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t* p) {
-    int32_t v;
-    asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
 
-// Receive buffer of one rank: flags [2][P] int32 (padded to 64 bytes), then
-// [2][P][stride] f32 record blocks.
-__host__ __device__ inline size_t ex_flag_bytes(int P) { return ((size_t)2 * P * 4 + 63) & ~(size_t)63; }
+// words per row: D + 4 record floats and the argmax
+__host__ __device__ constexpr int ex_row_words(int D) { return D + 5; }
 
+// Receive buffer of one rank: [2 parities][P ranks][N rows][D + 5] tagged
+// 8-byte words (low half: the value's bits, high half: the sequence number).
 template <int D>
 __global__ void __launch_bounds__(kExThreads)
     exchange_combine_kernel(int P, int rank, int N, int64_t stride, const float* __restrict__ local,
-                            const uint64_t* __restrict__ peers, uint8_t* __restrict__ mine,
+                            const uint64_t* __restrict__ peers, uint64_t* __restrict__ mine,
                             int32_t* __restrict__ state, float margin, uint16_t* __restrict__ out,
                             int32_t* __restrict__ flags, int32_t* __restrict__ tokens) {
+    constexpr int RW = ex_row_words(D);
     const int n = blockIdx.x, tid = threadIdx.x;
     __shared__ int sh_seq;
+    __shared__ float rec[kExMaxRanks][RW];
     if (tid == 0) sh_seq = *reinterpret_cast<volatile int32_t*>(state) + 1;
     __syncthreads();
     const int seq = sh_seq, par = seq & 1;
-    const size_t fb = ex_flag_bytes(P);
-    // 1. this block's share of the local block -> slot `rank` of every rank
-    const int64_t v4 = stride / 4;
-    const float4* src = reinterpret_cast<const float4*>(local);
-    for (int r = 0; r < P; ++r) {
-        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<uint8_t*>(peers[r]) + fb) +
-                      ((int64_t)par * P + rank) * v4;
-        for (int64_t i = (int64_t)n * kExThreads + tid; i < v4; i += (int64_t)gridDim.x * kExThreads)
-            dst[i] = src[i];
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (tid == 0) {
-        const int old = atomicAdd(state + 1, 1);
-        if (old == (int)gridDim.x - 1) {
-            state[1] = 0;
-            __threadfence_system();
-            for (int r = 0; r < P; ++r)
-                st_release_sys(reinterpret_cast<int32_t*>(peers[r]) + par * P + rank, seq);
+    const uint64_t tag = (uint64_t)(uint32_t)seq << 32;
+    const float* lrow = local + (int64_t)n * (D + 4);
+    const int32_t larg = reinterpret_cast<const int32_t*>(local + (int64_t)N * (D + 4))[n];
+    // 1. send row n to every rank
+    for (int w = tid; w < RW; w += kExThreads) {
+        const uint32_t bits = w < D + 4 ? __float_as_uint(lrow[w]) : (uint32_t)larg;
+        const uint64_t word = tag | bits;
+        for (int r = 0; r < P; ++r) {
+            uint64_t* dst = reinterpret_cast<uint64_t*>(peers[r]) +
+                            (((int64_t)par * P + rank) * N + n) * RW + w;
+            st_relaxed_sys_u64(dst, word);
         }
     }
-    // 2. wait for every rank's block of this step
-    const int32_t* myflags = reinterpret_cast<const int32_t*>(mine) + par * P;
-    if (tid < P) {
-        uint32_t i = 0;
-        while (ld_acquire_sys(myflags + tid) != seq) {
-            if (++i > kExSpinLimit) {
-                atomicExch(state + 3, FKV_ERR_TIMEOUT);
-                break;
+    // 2. receive row n of every rank (bounded polls)
+    for (int w = tid; w < RW; w += kExThreads) {
+        for (int k = 0; k < P; ++k) {
+            const uint64_t* src = mine + (((int64_t)par * P + k) * N + n) * RW + w;
+            uint64_t v = ld_relaxed_sys_u64(src);
+            uint32_t i = 0;
+            while ((uint32_t)(v >> 32) != (uint32_t)seq) {
+                if (++i > kExSpinLimit) {
+                    atomicExch(state + 3, FKV_ERR_TIMEOUT);
+                    break;
+                }
+                __nanosleep(32);
+                v = ld_relaxed_sys_u64(src);
             }
-            __nanosleep(32);
+            rec[k][w] = __uint_as_float((uint32_t)v);
         }
     }
     __syncthreads();
-    __threadfence();
-    // 3. merge row n over the P blocks in rank order
-    const float* blocks = reinterpret_cast<const float*>(mine + fb) + (int64_t)par * P * stride;
-    const int64_t rs = D + 4;
-    const int64_t argoff = (int64_t)N * rs;
+    // 3. merge the P records of row n in rank order
     float M = -INFINITY;
-    for (int k = 0; k < P; ++k) M = fmaxf(M, blocks[k * stride + n * rs]);
+    for (int k = 0; k < P; ++k) M = fmaxf(M, rec[k][0]);
     for (int d = tid; d < D; d += kExThreads) {
         float L = 0.f, acc = 0.f;
         if (M != -INFINITY) {
             for (int k = 0; k < P; ++k) {
-                const float* rec = blocks + k * stride + n * rs;
-                if (rec[0] == -INFINITY) continue;
-                const float wgt = exp2f((rec[0] - M) * kLog2e);
-                L = fmaf(wgt, rec[1], L);
-                acc = fmaf(wgt, rec[4 + d], acc);
+                if (rec[k][0] == -INFINITY) continue;
+                const float wgt = exp2f((rec[k][0] - M) * kLog2e);
+                L = fmaf(wgt, rec[k][1], L);
+                acc = fmaf(wgt, rec[k][4 + d], acc);
             }
         }
         out[(int64_t)n * D + d] = __half_as_ushort(__float2half_rn(L > 0.f ? acc / L : 0.f));
@@ -124,11 +122,10 @@ __global__ void __launch_bounds__(kExThreads)
         float mn = INFINITY, mf = -INFINITY;
         int af = -1;
         for (int k = 0; k < P; ++k) {
-            const float* rec = blocks + k * stride + n * rs;
-            mn = fminf(mn, rec[2]);
-            if (rec[3] > mf) {   // rank order: the first rank with the strict max wins
-                mf = rec[3];
-                af = reinterpret_cast<const int32_t*>(blocks + k * stride + argoff)[n];
+            mn = fminf(mn, rec[k][2]);
+            if (rec[k][3] > mf) {   // rank order: the first rank with the strict max wins
+                mf = rec[k][3];
+                af = __float_as_int(rec[k][D + 4]);
             }
         }
         flags[n] = (mf > mn + margin) ? 1 : 0;
@@ -163,8 +160,7 @@ extern "C" {
 
 size_t fkv_exchange_recv_bytes(int32_t P, int32_t N, int32_t D) {
     if (P <= 0 || N <= 0 || (D != 64 && D != 128)) return 0;
-    const int64_t stride = ((int64_t)N * (D + 4) + N + 3) & ~(int64_t)3;
-    return ex_flag_bytes(P) + (size_t)2 * P * stride * sizeof(float);
+    return (size_t)2 * P * N * ex_row_words(D) * sizeof(uint64_t);
 }
 
 int64_t fkv_exchange_block_stride(int32_t N, int32_t D) {
@@ -211,8 +207,8 @@ int fkv_exchange_combine(int32_t P, int32_t rank, int32_t N, int32_t D, const fl
                          const uint64_t* peer_recv, void* my_recv, int32_t* state, float spike_margin,
                          uint16_t* out, int32_t* flags, int32_t* tokens, void* stream) {
     fkv::clear_error();
-    FKV_REQUIRE(P > 0 && rank >= 0 && rank < P && N > 0, FKV_ERR_INVALID,
-                "fkv_exchange_combine: P=%d rank=%d N=%d", P, rank, N);
+    FKV_REQUIRE(P > 0 && P <= kExMaxRanks && rank >= 0 && rank < P && N > 0, FKV_ERR_INVALID,
+                "fkv_exchange_combine: P=%d (at most %d) rank=%d N=%d", P, kExMaxRanks, rank, N);
     FKV_REQUIRE(D == 64 || D == 128, FKV_ERR_UNSUPPORTED, "head dim %d unsupported", D);
     FKV_REQUIRE(local_block && peer_recv && my_recv && state && out && flags && tokens,
                 FKV_ERR_INVALID, "fkv_exchange_combine: NULL argument");
@@ -229,11 +225,11 @@ int fkv_exchange_combine(int32_t P, int32_t rank, int32_t N, int32_t D, const fl
     cudaStream_t st = (cudaStream_t)stream;
     if (D == 128)
         exchange_combine_kernel<128><<<N, kExThreads, 0, st>>>(P, rank, N, stride, local_block, peer_recv,
-                                                             static_cast<uint8_t*>(my_recv), state,
+                                                             static_cast<uint64_t*>(my_recv), state,
                                                              spike_margin, out, flags, tokens);
     else
         exchange_combine_kernel<64><<<N, kExThreads, 0, st>>>(P, rank, N, stride, local_block, peer_recv,
-                                                            static_cast<uint8_t*>(my_recv), state,
+                                                            static_cast<uint64_t*>(my_recv), state,
                                                             spike_margin, out, flags, tokens);
     FKV_LAUNCH_CHECK();
     return FKV_OK;

@@ -281,16 +281,17 @@ int fkv_combine_partials_strided(int32_t P, int32_t N, int32_t D, const float* p
  * sequence-split step with one launch per rank that stores this rank's
  * [records | argmax] block (fkv_decode_fp8_partial's layout, padded to
  * fkv_exchange_block_stride floats, 16-byte aligned) into slot `rank` of
- * every rank's receive buffer with plain peer stores, publishes a sequence
- * number in every rank's flag for it, waits (bounded) for all P flags of its
- * own buffer and merges row n of the P blocks in rank order, exactly as
- * fkv_combine_partials.
+ * every rank's receive buffer with plain peer stores, each word tagged with
+ * the step's sequence number in one 8-byte store, polls (bounded) its own
+ * buffer until every rank's rows carry the tag, and merges the P records of
+ * each row in rank order, exactly as fkv_combine_partials.
  *   peer_recv  device array of P receive-buffer addresses (own included),
  *              each fkv_exchange_recv_bytes long, zero-filled once, 64-byte
  *              aligned; peers' buffers mapped with fkv_ipc_open
- *   state      4 int32 of this rank, zero-filled once: sequence number, two
- *              block counters, status (FKV_ERR_TIMEOUT if a peer's block did
- *              not arrive in about half a second)
+ *   state      4 int32 of this rank, zero-filled once: sequence number, a
+ *              block counter, unused, status (FKV_ERR_TIMEOUT if a peer's
+ *              rows did not arrive in under a second)
+ * At most 8 ranks.
  * Every rank must issue the same sequence of calls; one rank per GPU.
  * The receive buffers alternate between two halves by step parity. */
 size_t fkv_exchange_recv_bytes(int32_t P, int32_t N, int32_t D);
