@@ -915,6 +915,7 @@ __device__ __forceinline__ void turbo_qproj_gather(const DecodeParams& p, int cr
 // split records (bandwidth- instead of latency-bound for many splits).
 constexpr int kMaxSplits = 64;
 constexpr int kDirectMerge = 10;   // split counts merged with direct loads
+constexpr int kMergeGroup = 8;     // first-level group of the two-level merge
 constexpr int kMergeScratch = (kMaxSplits * 40 + kMaxSplits * 8 + 8) * 4;   // bytes
 
 template <bool G>
@@ -923,9 +924,13 @@ __device__ __forceinline__ float4 ld4(const float* a) {
     else return *reinterpret_cast<const float4*>(a);
 }
 
+// grec != nullptr: instead of the outputs, the merged record of all 8 heads
+// (RecLayout, o unnormalised) is written there -- the first level of a
+// two-level merge
 template <int D, bool FROM_GLOBAL>
 __device__ __forceinline__ void merge_heads(const DecodeParams& p, const float* recs, int n,
-                                            int stride, int s, int hg, float* __restrict__ scratch) {
+                                            int stride, int s, int hg, float* __restrict__ scratch,
+                                            float* __restrict__ grec = nullptr) {
     using R = RecLayout<D>;
     static_assert(kConsumerThreads == 128, "merge layout: 16 threads per head");
     const int tid = threadIdx.x;
@@ -974,7 +979,13 @@ __device__ __forceinline__ void merge_heads(const DecodeParams& p, const float* 
     const int g = hg * kHeadsPerTile + head;
     if (sub == 0) {
         hl[head] = L;
-        if (g < p.G) {
+        if (grec != nullptr) {
+            grec[R::M + head] = M;
+            grec[R::L + head] = L;
+            grec[R::MN + head] = mn;
+            grec[R::MF + head] = mf;
+            grec[R::AF + head] = __int_as_float(af);
+        } else if (g < p.G) {
             const int64_t bh = (int64_t)b * p.Hq + (int64_t)h * p.G + g;
             if (p.part != nullptr) {
                 *reinterpret_cast<float4*>(p.part + bh * (D + 4)) = make_float4(M, L, mn, mf);
@@ -1006,10 +1017,19 @@ __device__ __forceinline__ void merge_accumulate(float (&acc)[8 * D / kConsumerT
 // thread's E contiguous outputs -> out (fp16, divided by L) or the partial record
 template <int D>
 __device__ __forceinline__ void merge_emit(const DecodeParams& p, const float (&acc)[8 * D / kConsumerThreads],
-                                          int s, int hg, const float* __restrict__ scratch) {
+                                          int s, int hg, const float* __restrict__ scratch,
+                                          float* __restrict__ grec = nullptr) {
+    using R = RecLayout<D>;
     constexpr int E = 8 * D / kConsumerThreads;
     const float* hl = scratch + kMaxSplits * 40 + kMaxSplits * 8;
     const int e0 = threadIdx.x * E, head = e0 / D, d0 = e0 % D;
+    if (grec != nullptr) {
+#pragma unroll
+        for (int j = 0; j < E / 4; ++j)
+            *reinterpret_cast<float4*>(grec + R::O + e0 + 4 * j) =
+                make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+        return;
+    }
     const int g = hg * kHeadsPerTile + head;
     if (g >= p.G) return;
     const int b = s / p.Hk, h = s % p.Hk;
@@ -1054,7 +1074,8 @@ __device__ __forceinline__ void merge_warps(const DecodeParams& p, const float* 
 // time into two shared-memory buffers (mbar[0], mbar[1]) behind the scratch
 template <int D>
 __device__ __forceinline__ void merge_splits(const DecodeParams& p, const float* base, int n, int s,
-                                            int hg, uint8_t* smem, uint64_t* mbar) {
+                                            int hg, uint8_t* smem, uint64_t* mbar,
+                                            float* grec = nullptr) {
     using R = RecLayout<D>;
     constexpr int E = 8 * D / kConsumerThreads;
     constexpr int RB = R::SIZE * 4;                      // record bytes (multiple of 16)
@@ -1074,7 +1095,7 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, const float*
 #pragma unroll
             for (int j = 0; j < E4; ++j)
                 if (u < n) v[u][j] = ld4<true>(base + u * R::SIZE + R::O + e0 + 4 * j);
-        merge_heads<D, true>(p, base, n, R::SIZE, s, hg, scratch);
+        merge_heads<D, true>(p, base, n, R::SIZE, s, hg, scratch, grec);
         const float* wk = scratch + kMaxSplits * 40;
         const int head = e0 / D;
         float acc[E4 * 4];
@@ -1093,7 +1114,7 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, const float*
                 }
             }
         }
-        merge_emit<D>(p, acc, s, hg, scratch);
+        merge_emit<D>(p, acc, s, hg, scratch, grec);
         return;
     }
     const int nb = (n + kMergeBatch - 1) / kMergeBatch;
@@ -1110,7 +1131,7 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, const float*
         fence_proxy_async();
         for (int bi = 0; bi < min(nb, 2); ++bi) issue(bi);
     }
-    merge_heads<D, true>(p, base, n, R::SIZE, s, hg, scratch);
+    merge_heads<D, true>(p, base, n, R::SIZE, s, hg, scratch, grec);
     const float* wk = scratch + kMaxSplits * 40;
     const int e0 = threadIdx.x * E, head = e0 / D;
     float acc[E];
@@ -1125,7 +1146,7 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, const float*
         named_sync(1, kConsumerThreads);   // buffer (bi & 1) is free again
         if (threadIdx.x == 0 && bi + 2 < nb) issue(bi + 2);
     }
-    merge_emit<D>(p, acc, s, hg, scratch);
+    merge_emit<D>(p, acc, s, hg, scratch, grec);
 }
 
 // Cluster mode: merge the csize CTA records of one cluster (each in its CTA's
@@ -1805,8 +1826,45 @@ __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
     }
     __threadfence();
     named_sync(1, kConsumerThreads);
+    const int64_t unit = (int64_t)s * p.HG + hg;
+    uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR);
+    if (p.splits > kDirectMerge) {
+        // two-level merge: the last CTA of each group of kMergeGroup splits
+        // merges them into a group record (one round of loads), the last
+        // group merges the group records -- instead of one CTA streaming
+        // every split record through shared memory
+        const int ngrp = (p.splits + kMergeGroup - 1) / kMergeGroup;
+        const int grp = split / kMergeGroup;
+        const int gn = min(kMergeGroup, p.splits - grp * kMergeGroup);
+        const int64_t units = (int64_t)gridDim.y * gridDim.z;
+        if (threadIdx.x == 0) {
+            int* tk = p.tickets + units + unit * ngrp + grp;
+            const int old = atomicAdd(tk, 1);
+            sh_last = (old == gn - 1);
+            if (sh_last) *tk = 0;
+        }
+        named_sync(1, kConsumerThreads);
+        if (!sh_last) return;
+        __threadfence();
+        float* grecs = p.ws + units * p.splits * R::SIZE + unit * ngrp * R::SIZE;
+        merge_splits<D>(p, p.ws + (unit * p.splits + grp * kMergeGroup) * R::SIZE, gn, s, hg, smem, mbar,
+                        grecs + grp * R::SIZE);
+        __threadfence();
+        named_sync(1, kConsumerThreads);
+        if (threadIdx.x == 0) {
+            int* tk = p.tickets + unit;
+            const int old = atomicAdd(tk, 1);
+            sh_last = (old == ngrp - 1);
+            if (sh_last) *tk = 0;
+        }
+        named_sync(1, kConsumerThreads);
+        if (!sh_last) return;
+        __threadfence();
+        merge_splits<D>(p, grecs, ngrp, s, hg, smem, mbar);
+        return;
+    }
     if (threadIdx.x == 0) {
-        int* tk = p.tickets + ((int64_t)s * p.HG + hg);
+        int* tk = p.tickets + unit;
         const int old = atomicAdd(tk, 1);
         sh_last = (old == p.splits - 1);
         if (sh_last) *tk = 0;   // every other CTA of this stream has arrived
@@ -1814,8 +1872,8 @@ __global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
     named_sync(1, kConsumerThreads);
     if (!sh_last) return;
     __threadfence();
-    const float* base = p.ws + ((int64_t)s * p.HG + hg) * p.splits * R::SIZE;
-    merge_splits<D>(p, base, p.splits, s, hg, smem, reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR));
+    const float* base = p.ws + unit * p.splits * R::SIZE;
+    merge_splits<D>(p, base, p.splits, s, hg, smem, mbar);
 }
 
 // shard k's record n at parts + k * prs + n * (D + 4), its argmax at
@@ -2088,8 +2146,12 @@ Plan make_plan(const FkvDecodeShape* sh, int resident, bool turbo = false) {
     pl.splits = (int)std::max<int64_t>(1, (T + chunk - 1) / chunk);
     pl.chunk = (int)chunk;
     const int D = sh->D;
-    pl.rec_bytes = pl.splits > 1 ? (size_t)streams * pl.splits * (40 + 8 * D) * sizeof(float) : 0;
-    pl.ticket_bytes = 16 + (size_t)streams * sizeof(int32_t);   // status word + counters
+    // split records, then (more than kDirectMerge splits) the group records
+    // of the two-level merge; status word + one counter per stream, then the
+    // group counters
+    const int64_t ngrp = pl.splits > kDirectMerge ? (pl.splits + kMergeGroup - 1) / kMergeGroup : 0;
+    pl.rec_bytes = pl.splits > 1 ? (size_t)streams * (pl.splits + ngrp) * (40 + 8 * D) * sizeof(float) : 0;
+    pl.ticket_bytes = 16 + (size_t)streams * (1 + ngrp) * sizeof(int32_t);
     pl.qproj_bytes = (size_t)sh->B * sh->Hq * 2 * D * sizeof(float);
     return pl;
 }
