@@ -1253,7 +1253,7 @@ __device__ __forceinline__ void cluster_merge(const DecodeParams& p, int s, int 
 // the test hook p.test_stall is honoured; without RT both are compile-time
 // (the fixed limit, no hook), which keeps the hot loop's registers down.
 template <int D, int VG, int NH = 0, bool CL = false, bool RT = false>
-__global__ void __maxnreg__((NH > 0 || CL) ? 128 : 136)
+__global__ void __maxnreg__(128)
     decode_fp8_kernel(const DecodeParams p, const __grid_constant__ TMaps maps) {
     using R = RecLayout<D>;
     using RG = Ring<D, VG>;
