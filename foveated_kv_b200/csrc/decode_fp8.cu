@@ -1253,7 +1253,7 @@ __device__ __forceinline__ void cluster_merge(const DecodeParams& p, int s, int 
 // the test hook p.test_stall is honoured; without RT both are compile-time
 // (the fixed limit, no hook), which keeps the hot loop's registers down.
 template <int D, int VG, int NH = 0, bool CL = false, bool RT = false>
-__global__ void __maxnreg__(128)
+__global__ void __maxnreg__((NH > 0 || CL || VG == kTurbo) ? 128 : 136)
     decode_fp8_kernel(const DecodeParams p, const __grid_constant__ TMaps maps) {
     using R = RecLayout<D>;
     using RG = Ring<D, VG>;
@@ -1828,8 +1828,10 @@ __global__ void __maxnreg__(128)
     named_sync(1, kConsumerThreads);
     const int64_t unit = (int64_t)s * p.HG + hg;
     uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR);
-    if (p.splits > kDirectMerge) {
-        // two-level merge: the last CTA of each group of kMergeGroup splits
+    if (VG == kTurbo && p.splits > kDirectMerge) {
+        // two-level merge (TurboQuant tier, whose small streams take many
+        // splits; in the fp8 kernels the extra code cost the hot loop
+        // registers and c3 4 %): the last CTA of each group of kMergeGroup splits
         // merges them into a group record (one round of loads), the last
         // group merges the group records -- instead of one CTA streaming
         // every split record through shared memory
@@ -2149,7 +2151,7 @@ Plan make_plan(const FkvDecodeShape* sh, int resident, bool turbo = false) {
     // split records, then (more than kDirectMerge splits) the group records
     // of the two-level merge; status word + one counter per stream, then the
     // group counters
-    const int64_t ngrp = pl.splits > kDirectMerge ? (pl.splits + kMergeGroup - 1) / kMergeGroup : 0;
+    const int64_t ngrp = turbo && pl.splits > kDirectMerge ? (pl.splits + kMergeGroup - 1) / kMergeGroup : 0;
     pl.rec_bytes = pl.splits > 1 ? (size_t)streams * (pl.splits + ngrp) * (40 + 8 * D) * sizeof(float) : 0;
     pl.ticket_bytes = 16 + (size_t)streams * (1 + ngrp) * sizeof(int32_t);
     pl.qproj_bytes = (size_t)sh->B * sh->Hq * 2 * D * sizeof(float);
@@ -2436,11 +2438,13 @@ size_t fkv_decode_workspace_bytes(const FkvDecodeShape* s) {
     const Plan a = make_plan(s, resident_for(s, false)), b = make_plan(s, resident_for(s, true), true);
     const Plan c = make_plan(s, resident_for(s, false, 0));
     const Plan d = make_cl_plan(s, false), e = make_cl_plan(s, true);
-    const Plan& ab = a.rec_bytes >= b.rec_bytes ? a : b;
-    const Plan& de = d.rec_bytes >= e.rec_bytes ? d : e;
-    const Plan& abd = ab.rec_bytes >= de.rec_bytes ? ab : de;
-    const Plan& pl = abd.rec_bytes >= c.rec_bytes ? abd : c;
-    return pl.rec_bytes + pl.ticket_bytes + 256 + ((pl.qproj_bytes + 255) & ~(size_t)255) + 256;
+    size_t rec = 0, tick = 0, qp = 0;
+    for (const Plan* pl : {&a, &b, &c, &d, &e}) {
+        rec = std::max(rec, pl->rec_bytes);
+        tick = std::max(tick, pl->ticket_bytes);
+        qp = std::max(qp, pl->qproj_bytes);
+    }
+    return rec + tick + 256 + ((qp + 255) & ~(size_t)255) + 256;
 }
 
 int fkv_decode_status(const void* workspace, int32_t* status, int32_t clear, void* stream) {
