@@ -78,12 +78,6 @@ __device__ __forceinline__ uint32_t nib2hi_to_h2(uint32_t x) {
     return h2_as_u32(__hsub2(u32_as_h2(magic), u32_as_h2(0x54005400u)));
 }
 
-// high nibbles as 64 + code, without the subtraction (the caller removes
-// 64 * sum(p * scale) once): 0x5400 | (c << 4) is exactly 64 + c
-__device__ __forceinline__ uint32_t nib2hi_plus64(uint32_t x) {
-    return (x & 0x00F000F0u) | 0x54005400u;
-}
-
 // dequant v = code * scale + zero in fp16 arithmetic (two roundings, as the
 // reference's _dequant_int4_per_token does in fp16)
 __device__ __forceinline__ uint32_t dq_h2(uint32_t codes, uint32_t s2, uint32_t z2) {
@@ -127,8 +121,6 @@ struct WarpState {
     float m;        // running max of head r (natural-log units)
     float l;        // partial denominator (this lane's tokens)
     float z;        // partial sum of p * zero (per-token INT4 zero folded out of V)
-    float y;        // partial sum of fp16(p * scale): the high-nibble codes enter the
-                    // P.V product as 64 + code, removed once per record as 64 * y
     float mn;       // min near/decode score, head r
     float mf;       // max far score, head r
     int af;         // argmax far (far-local index), head r
@@ -139,7 +131,6 @@ struct WarpState {
         m = -INFINITY;
         l = 0.f;
         z = 0.f;
-        y = 0.f;
         mn = INFINITY;
         mf = -INFINITY;
         af = -1;
@@ -162,7 +153,6 @@ struct WarpState {
             const float alpha = (m == -INFINITY) ? 0.f : exp2f((m - mnew) * kLog2e);
             l *= alpha;
             z *= alpha;
-            y *= alpha;
             m = mnew;
             const int c = lane & 3;
             const float a0 = __shfl_sync(0xffffffffu, alpha, (2 * c) * 4);

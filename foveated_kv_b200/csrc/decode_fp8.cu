@@ -463,11 +463,6 @@ __device__ __forceinline__ void far_tail(const float (&sv)[4 * NT],
             }
             pb0 = pack_h2(ps[0], ps[1]);
             pb1 = pack_h2(ps[2], ps[3]);
-            {
-                // the fp16 weights exactly as the tensor core sees them
-                const float2 w0 = __half22float2(u32_as_h2(pb0)), w1 = __half22float2(u32_as_h2(pb1));
-                st.y += (w0.x + w0.y) + (w1.x + w1.y);
-            }
 #pragma unroll
             for (int i = 0; i < D / 16; ++i) {
                 const int wi = i >> 2, bi = i & 3;
@@ -476,9 +471,9 @@ __device__ __forceinline__ void far_tail(const float (&sv)[4 * NT],
                 const uint32_t xcd = prmt(vr[t][2][wi], vr[t][3][wi], sel);
                 uint32_t a[4];
                 a[0] = nib2_to_h2(xab);
-                a[1] = nib2hi_plus64(xab);   // odd dims: 64 + code
+                a[1] = nib2hi_to_h2(xab);
                 a[2] = nib2_to_h2(xcd);
-                a[3] = nib2hi_plus64(xcd);
+                a[3] = nib2hi_to_h2(xcd);
                 mma16816(st.o[i], a, pb0, pb1);
             }
         } else {
@@ -1726,10 +1721,6 @@ __global__ void __maxnreg__((NH > 0 || CL || VG == kTurbo) ? 128 : 136)
     quad_argmax(st.mf, st.af);
     const float z0 = __shfl_sync(0xffffffffu, st.z, (2 * c) * 4);
     const float z1 = __shfl_sync(0xffffffffu, st.z, (2 * c + 1) * 4);
-    st.y = quad_sum(st.y);
-    // odd dims carried 64 + code in the far P.V products of per-token V
-    const float y0 = z0 - 64.f * __shfl_sync(0xffffffffu, st.y, (2 * c) * 4);
-    const float y1 = z1 - 64.f * __shfl_sync(0xffffffffu, st.y, (2 * c + 1) * 4);
     named_sync(1, kConsumerThreads);
     float* sh_rec = reinterpret_cast<float*>(smem);
     float* wr = sh_rec + w * R::SIZE;
@@ -1745,8 +1736,8 @@ __global__ void __maxnreg__((NH > 0 || CL || VG == kTurbo) ? 128 : 136)
         const int d0 = r * (D / 8) + 2 * i;
         wr[R::O + (2 * c) * D + d0] = st.o[i][0] + z0;
         wr[R::O + (2 * c + 1) * D + d0] = st.o[i][1] + z1;
-        wr[R::O + (2 * c) * D + d0 + 1] = st.o[i][2] + y0;
-        wr[R::O + (2 * c + 1) * D + d0 + 1] = st.o[i][3] + y1;
+        wr[R::O + (2 * c) * D + d0 + 1] = st.o[i][2] + z0;
+        wr[R::O + (2 * c + 1) * D + d0 + 1] = st.o[i][3] + z1;
     }
     named_sync(1, kConsumerThreads);
     if constexpr (UM) {
