@@ -206,3 +206,62 @@ def test_c4_long_split_eight_shards(c4_long, qk_path):
     assert ties == 0
     assert np_(fl).all()
     print(f"c4 256K split x{P} {qk_path}: max-abs {err:.2e} cos {cos:.7f}")
+
+
+# ---- full-size properties (the oracle cannot finish these sizes quickly) -----------
+
+def test_c3_full_batch_rows_match_slices():
+    """c3 at its full size (B = 64, S = 32K, with the injected spikes): every
+    sequence's outputs, flags and tokens from the 64-sequence launch equal
+    those of the same sequence decoded in a 2-sequence launch (batch rows are
+    independent), within the parity tolerance; the slices themselves are
+    oracle-checked above."""
+    from foveated_kv_b200.synthetic import torch_workload, inject_spikes_torch
+    c = _cfg("c3")
+    cfg = _tier_cfg(c)
+    w = torch_workload(91, c["B"], c["Hk"], c["Hq"], c["S"], c["D"], 0, "cuda")
+    inject_spikes_torch(w, cfg.tier_boundaries(c["S"]), 91)
+    full = compress_layer(w["k"], w["v"], cfg, keep_archive=False)
+    out, fl, tk = full.attend_fused_with_spikes(w["q"])
+    out, fl, tk = out.clone(), fl.clone(), tk.clone()
+    del full
+    for b0 in (0, 30, 62):
+        part = compress_layer(w["k"][b0:b0 + 2], w["v"][b0:b0 + 2], cfg, keep_archive=False)
+        o2, f2, t2 = part.attend_fused_with_spikes(w["q"][b0:b0 + 2])
+        torch.cuda.synchronize()
+        err = (o2.float() - out[b0:b0 + 2].float()).abs().max().item()
+        assert err <= 2e-3, (b0, err)
+        assert torch.equal(f2, fl[b0:b0 + 2]) and torch.equal(t2, tk[b0:b0 + 2])
+        del part
+    assert bool(fl.all())
+
+
+@pytest.mark.parametrize("P", [2, 8])
+def test_c4_full_million_split_equals_unsplit(P):
+    """c4 at its full length (S = 2^20, Hq32/Hk8, 5% near): the sequence split
+    into P equal-cost shards on one GPU (partial kernel per shard + merge)
+    equals the unsplit fused decode of the whole sequence within the parity
+    tolerance, with identical flags and tokens (global far indices)."""
+    from foveated_kv_b200.synthetic import torch_workload
+    from foveated_kv_b200.seqsplit import shard_bounds_balanced, compress_shard, decode_partial, combine
+    c = _cfg("c4")
+    B, Hq, Hk, D, S = c["B"], c["Hq"], c["Hk"], c["D"], c["S"]
+    cfg = _tier_cfg(c)
+    w = torch_workload(92, B, Hk, Hq, S, D, 0, "cuda")
+    full = compress_layer(w["k"], w["v"], cfg, keep_archive=False)
+    ro, rf, rt = full.attend_fused_with_spikes(w["q"])
+    ro, rf, rt = ro.clone(), rf.clone(), rt.clone()
+    del full
+    parts, args = [], []
+    for r in range(P):
+        lo, hi = shard_bounds_balanced(S, r, P, cfg)
+        lay, off = compress_shard(w["k"][:, :, lo:hi], w["v"][:, :, lo:hi], S, lo, cfg)
+        pa, ar = decode_partial(lay, w["q"], off)
+        parts.append(pa.clone())
+        args.append(ar.clone())
+        del lay
+    out, fl, tk = combine(torch.stack(parts), torch.stack(args), 0.5)
+    torch.cuda.synchronize()
+    err = (out.float() - ro.float().reshape(out.shape)).abs().max().item()
+    assert err <= 2e-3, err
+    assert torch.equal(fl, rf.reshape(-1)) and torch.equal(tk, rt.reshape(-1))
