@@ -87,19 +87,26 @@ __global__ void __launch_bounds__(kExThreads)
     }
     // 2. receive row n of every rank (bounded polls)
     for (int w = tid; w < RW; w += kExThreads) {
-        for (int k = 0; k < P; ++k) {
+        // one round of loads for all ranks first, then re-poll the words
+        // that have not arrived yet
+        uint64_t v[kExMaxRanks];
+#pragma unroll
+        for (int k = 0; k < kExMaxRanks; ++k)
+            if (k < P) v[k] = ld_relaxed_sys_u64(mine + (((int64_t)par * P + k) * N + n) * RW + w);
+#pragma unroll
+        for (int k = 0; k < kExMaxRanks; ++k) {
+            if (k >= P) continue;
             const uint64_t* src = mine + (((int64_t)par * P + k) * N + n) * RW + w;
-            uint64_t v = ld_relaxed_sys_u64(src);
             uint32_t i = 0;
-            while ((uint32_t)(v >> 32) != (uint32_t)seq) {
+            while ((uint32_t)(v[k] >> 32) != (uint32_t)seq) {
                 if (++i > kExSpinLimit) {
                     atomicExch(state + 3, FKV_ERR_TIMEOUT);
                     break;
                 }
                 __nanosleep(32);
-                v = ld_relaxed_sys_u64(src);
+                v[k] = ld_relaxed_sys_u64(src);
             }
-            rec[k][w] = __uint_as_float((uint32_t)v);
+            rec[k][w] = __uint_as_float((uint32_t)v[k]);
         }
     }
     __syncthreads();
