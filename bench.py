@@ -532,15 +532,19 @@ def main_seqsplit(args, rank, world, device):
     for _ in range(max(args.warmup, 3)):
         step()
     torch.cuda.synchronize()
+    # the sampler starts (NVML set-up takes milliseconds) before the barrier,
+    # so every rank enters the timed region together: the ranks wait on each
+    # other inside the exchange, and a late start would be timed as steps
+    clk = ClockSampler(int(os.environ.get("LOCAL_RANK", 0))).__enter__()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(int(os.environ.get("LOCAL_RANK", 0))) as clk:
-        e0.record()
-        for _ in range(args.steps):
-            step()
-        e1.record()
-        torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    clk.__exit__(None, None, None)
     ms = e0.elapsed_time(e1) / (args.steps * per)
     nv_sum = int(lay.near_valid.sum().item())
     alg_local = algorithmic_bytes(B, Hq, Hk, D, nv_sum, lay.n_far, 0)
@@ -666,7 +670,11 @@ def main():
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     cur = torch.cuda.current_stream()
-    with ClockSampler(local) as clk:
+    clk = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with clk:
         e0.record(cur)
         for _ in range(args.steps):
             graph.replay()
