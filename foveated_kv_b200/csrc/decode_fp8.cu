@@ -627,8 +627,10 @@ __device__ __forceinline__ bool far_tiles_um(uint8_t* __restrict__ kbuf,
 // TurboQuant far tier: scores directly on codes
 // ---------------------------------------------------------------------------
 // far score = (|k| * <q Pi^T, c[idx]> + qjl_coef/D * gamma * <q S^T, sign>) / sqrt(D)
-// (foveated_attn.metal:486-521,684-688).  c[idx] is written as a thermometer
-// sum c0 + (c1-c0)[idx>=1] + (c2-c1)[idx>=2] + (c3-c2)[idx>=3] and sign as
+// (foveated_attn.metal:486-521,684-688).  c[idx] is written through the
+// code's bits b0 (low), b1 as c0 + (c1-c0) b0 + (c2-c0) b1 + ((c3-c2)-(c1-c0))
+// b0 b1 (the last term is zero for the symmetric Lloyd-Max centroids and is
+// then skipped: two products per 16 dims instead of three) and sign as
 // 2[bit] - 1, so the tensor cores only see {0, 1} B fragments (exact in f16)
 // against hi/lo-split q Pi^T and q S^T fragments; the centroids and sums are
 // applied to the fp32 results.  Turbo K dimension permutation: k-step j, lane
@@ -787,9 +789,10 @@ __device__ __forceinline__ void turbo_tile(const uint8_t* __restrict__ sgn,
             const uint32_t x = (kr[n][j] >> (8 * c)) & 0xFFu;   // codes of dims 4(4j+c)+0..3
             const uint32_t y01 = x | (x << 14);                 // dim0 -> bits 0-1, dim1 -> 16-17
             const uint32_t y23 = (x >> 4) | (x << 10);          // dim2 -> bits 0-1, dim3 -> 16-17
-            mma16816(acc[0][n], ar, bits2_to_h2(y01 | (y01 >> 1)), bits2_to_h2(y23 | (y23 >> 1)));
-            mma16816(acc[1][n], ar, bits2_to_h2(y01 >> 1), bits2_to_h2(y23 >> 1));
-            mma16816(acc[2][n], ar, bits2_to_h2(y01 & (y01 >> 1)), bits2_to_h2(y23 & (y23 >> 1)));
+            mma16816(acc[0][n], ar, bits2_to_h2(y01), bits2_to_h2(y23));             // low bit
+            mma16816(acc[1][n], ar, bits2_to_h2(y01 >> 1), bits2_to_h2(y23 >> 1));   // high bit
+            if (cf[3] != 0.f)   // both bits (asymmetric centroids only; warp-uniform)
+                mma16816(acc[2][n], ar, bits2_to_h2(y01 & (y01 >> 1)), bits2_to_h2(y23 & (y23 >> 1)));
             const int sbyte = 2 * j + (c >> 1);                  // sign byte of these dims
             const uint32_t z = (sg[n][sbyte >> 2] >> (8 * (sbyte & 3) + 4 * (c & 1))) & 0xFu;
             mma16816(acc[3][n], ak, bits2_to_h2(z | (z << 15)), bits2_to_h2((z >> 2) | (z << 13)));
@@ -800,12 +803,12 @@ __device__ __forceinline__ void turbo_tile(const uint8_t* __restrict__ sgn,
     for (int j = 0; j < 4; ++j) {
         const int u = u0 + (j >> 1) * 8 + 2 * c + (j & 1);
         const int n = j >> 1, e = j & 1;
-        const float t1 = acc[0][n][e] + acc[0][n][2 + e];
-        const float t2 = acc[1][n][e] + acc[1][n][2 + e];
-        const float t3 = acc[2][n][e] + acc[2][n][2 + e];
+        const float b0 = acc[0][n][e] + acc[0][n][2 + e];
+        const float b1 = acc[1][n][e] + acc[1][n][2 + e];
+        const float b01 = acc[2][n][e] + acc[2][n][2 + e];
         const float sgn = acc[3][n][e] + acc[3][n][2 + e];
         const float2 f = __half22float2(u32_as_h2(ng[j]));      // (norm, gamma)
-        const float mse = fmaf(cf[3], t3, fmaf(cf[2], t2, fmaf(cf[1], t1, cf[0] * sum_r)));
+        const float mse = fmaf(cf[3], b01, fmaf(cf[2], b1, fmaf(cf[1], b0, cf[0] * sum_r)));
         const float qjl = cf[4] * f.y * fmaf(2.f, sgn, -sum_k);
         const float v = fmaf(f.x, mse, qjl) * cf[5];
         s[j] = u < cnt ? v : -INFINITY;
@@ -911,10 +914,12 @@ __device__ __forceinline__ void turbo_qproj_gather(const DecodeParams& p, int cr
 // weights exp(m_k - M), the denominators and the spike trackers.  The o
 // vectors are then accumulated by every thread over its 8 (D = 128) or 4
 // (D = 64) contiguous outputs: straight from shared memory for the per-warp
-// records, through double-buffered bulk copies (TMA) of whole records for the
-// split records (bandwidth- instead of latency-bound for many splits).
+// records, and for the split records with one round of direct loads (few
+// records, or few active heads) or through double-buffered bulk copies (TMA)
+// of whole records (bandwidth- instead of latency-bound for many splits).
 constexpr int kMaxSplits = 64;
 constexpr int kDirectMerge = 10;   // split counts merged with direct loads
+constexpr int kNarrowLoads = 8;    // records per thread in the few-heads merge
 constexpr int kMergeGroup = 8;     // first-level group of the two-level merge
 constexpr int kMergeScratch = (kMaxSplits * 40 + kMaxSplits * 8 + 8) * 4;   // bytes
 
@@ -1116,6 +1121,62 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, const float*
         }
         merge_emit<D>(p, acc, s, hg, scratch, grec);
         return;
+    }
+    {
+        // few active q heads in this head group (G < 8): only their nh x D
+        // outputs are merged.  They form CH float4 chunks; the threads split
+        // into RGN groups of CH, group gi taking records gi, gi + RGN, ...,
+        // every load issued before the scalar pass (one round of latency,
+        // no bulk-copy round trips), then the groups' sums are reduced
+        // through shared memory behind the scratch.
+        const int nh = min(kHeadsPerTile, p.G - hg * kHeadsPerTile);
+        const int CH = nh * D / 4;
+        const int RGN = CH <= kConsumerThreads ? kConsumerThreads / CH : 0;
+        if (grec == nullptr && RGN > 0 && n <= kNarrowLoads * RGN) {
+            const int c = threadIdx.x % CH, gi = threadIdx.x / CH;
+            const bool act = gi < RGN;
+            float4 v[kNarrowLoads];
+#pragma unroll
+            for (int j = 0; j < kNarrowLoads; ++j) {
+                const int u = gi + j * RGN;
+                if (act && u < n) v[j] = ld4<true>(base + u * R::SIZE + R::O + 4 * c);
+            }
+            merge_heads<D, true>(p, base, n, R::SIZE, s, hg, scratch);
+            const float* wk = scratch + kMaxSplits * 40;
+            const int head = (4 * c) / D;
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < kNarrowLoads; ++j) {
+                const int u = gi + j * RGN;
+                if (act && u < n) {
+                    const float wgt = wk[u * 8 + head];
+                    a.x = fmaf(wgt, v[j].x, a.x);
+                    a.y = fmaf(wgt, v[j].y, a.y);
+                    a.z = fmaf(wgt, v[j].z, a.z);
+                    a.w = fmaf(wgt, v[j].w, a.w);
+                }
+            }
+            float4* red = reinterpret_cast<float4*>(smem + BUF0);   // [RGN][CH]
+            if (act) red[gi * CH + c] = a;
+            named_sync(1, kConsumerThreads);
+            const int e0 = threadIdx.x * E;
+            float acc[E];
+#pragma unroll
+            for (int x = 0; x < E; ++x) acc[x] = 0.f;
+            if (e0 < nh * D) {
+#pragma unroll
+                for (int j = 0; j < E / 4; ++j) {
+                    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (int g = 0; g < RGN; ++g) {
+                        const float4 q = red[g * CH + e0 / 4 + j];
+                        t.x += q.x; t.y += q.y; t.z += q.z; t.w += q.w;
+                    }
+                    acc[4 * j] = t.x; acc[4 * j + 1] = t.y; acc[4 * j + 2] = t.z; acc[4 * j + 3] = t.w;
+                }
+            }
+            merge_emit<D>(p, acc, s, hg, scratch);
+            return;
+        }
     }
     const int nb = (n + kMergeBatch - 1) / kMergeBatch;
     auto issue = [&](int bi) {
@@ -1580,7 +1641,10 @@ __global__ void __maxnreg__((NH > 0 || CL || VG == kTurbo) ? 128 : 136)
     if constexpr (VG == kTurbo) {
         const float c0 = __ldg(p.centroids), c1 = __ldg(p.centroids + 1);
         const float c2 = __ldg(p.centroids + 2), c3 = __ldg(p.centroids + 3);
-        cf[0] = c0; cf[1] = c1 - c0; cf[2] = c2 - c1; cf[3] = c3 - c2;
+        // c[code] = c0 + (c1 - c0) b0 + (c2 - c0) b1 + ((c3 - c2) - (c1 - c0)) b0 b1
+        // for the code's bits b0 (low) and b1; the b0 b1 term vanishes for the
+        // symmetric Lloyd-Max centroids, and its tensor-core product with it
+        cf[0] = c0; cf[1] = c1 - c0; cf[2] = c2 - c0; cf[3] = (c3 - c2) - (c1 - c0);
         cf[4] = p.qjl_coef / (float)D;
         cf[5] = p.qscale;
         sum_r = tsum[lane >> 2];

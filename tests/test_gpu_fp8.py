@@ -196,6 +196,48 @@ def test_decode_buffer_growth_and_flags_all_set():
     assert np.array_equal(np_(tk), rtk)
 
 
+def _raw_decode(lay, sh, q, Hq, D):
+    """fkv_decode_fp8 through the C ABI with the shape as given (twice: the
+    second call reuses the workspace, whose counters the first put back)."""
+    lib = _native.load()
+    B = q.shape[0]
+    ws = torch.zeros(lib.fkv_decode_workspace_bytes(C.byref(sh)) + 16, dtype=torch.uint8,
+                     device=dev)
+    out = torch.empty((B, Hq, D), dtype=torch.float16, device=dev)
+    fl = torch.empty((B, Hq), dtype=torch.int32, device=dev)
+    tk = torch.empty_like(fl)
+    p = lambda x: x.data_ptr()
+    for _ in range(2):
+        rc = lib.fkv_decode_fp8(C.byref(sh), p(lay.near_k), p(lay.near_v), p(lay.near_valid),
+                                p(lay.far_k), p(lay.far_v), p(lay.far_v_scale),
+                                p(lay.far_v_zero), p(q), p(lay._dec_k), p(lay._dec_v),
+                                p(out), p(fl), p(tk), p(ws), ws.numel(),
+                                torch.cuda.current_stream().cuda_stream)
+        _native.check(rc, "fkv_decode_fp8")
+    torch.cuda.synchronize()
+    return out, fl, tk
+
+
+@pytest.mark.parametrize("G,D,splits", [(1, 128, 13), (1, 128, 32), (2, 128, 16), (1, 64, 60),
+                                         (4, 64, 16)])
+def test_decode_few_heads_many_splits(G, D, splits, qk_path):
+    """Streams with few q heads (G < 8) and more split records than the direct
+    merge takes: the last CTA merges only the active heads' outputs, spread
+    over thread groups that each take every k-th record."""
+    Hk, S = 2, 4000
+    w = numpy_workload(11, 1, Hk, G * Hk, S, D, 3)
+    t = _tensors(w)
+    lay = compress_layer(t["k"], t["v"], TierConfig())
+    for i in range(3):
+        lay.add_token(t["dec_k"][:, :, i:i + 1], t["dec_v"][:, :, i:i + 1])
+    sh = lay._fill_shape(G * Hk, 0.5)
+    sh.num_splits = splits
+    out, fl, tk = _raw_decode(lay, sh, t["q"], G * Hk, D)
+    rout, rfl, rtk, diag = O.decode_attend(layer_to_oracle(lay), w["q"], w["dec_k"], w["dec_v"], 0.5)
+    assert_output_close(np_(out).astype(np.float64), rout, f"G={G} D={D} splits={splits}")
+    assert assert_spikes_match(np_(fl), np_(tk), rfl, rtk, diag, 0.5) == 0
+
+
 @pytest.mark.parametrize("splits", [1, 0])
 def test_decode_long_stream_accumulation(splits, qk_path):
     """One 32K-token stream decoded by as few CTAs as possible (splits=1): the
