@@ -1892,10 +1892,11 @@ __global__ void __maxnreg__((NH > 0 || CL || VG == kTurbo) ? 128 : 136)
     named_sync(1, kConsumerThreads);
     const int64_t unit = (int64_t)s * p.HG + hg;
     uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + RG::MERGEBAR);
-    if (VG == kTurbo && p.splits > kDirectMerge) {
+    if ((VG == kTurbo || UM) && p.splits > kDirectMerge) {
         // two-level merge (TurboQuant tier, whose small streams take many
-        // splits; in the fp8 kernels the extra code cost the hot loop
-        // registers and c3 4 %): the last CTA of each group of kMergeGroup splits
+        // splits, and the tensor-core q.K kernels, which stay within their
+        // 128 registers with it; in the mma.sync fp8 kernels the extra code
+        // cost the hot loop registers and c3 4 %): the last CTA of each group of kMergeGroup splits
         // merges them into a group record (one round of loads), the last
         // group merges the group records -- instead of one CTA streaming
         // every split record through shared memory
@@ -2215,7 +2216,7 @@ Plan make_plan(const FkvDecodeShape* sh, int resident, bool turbo = false) {
     // split records, then (more than kDirectMerge splits) the group records
     // of the two-level merge; status word + one counter per stream, then the
     // group counters
-    const int64_t ngrp = turbo && pl.splits > kDirectMerge ? (pl.splits + kMergeGroup - 1) / kMergeGroup : 0;
+    const int64_t ngrp = pl.splits > kDirectMerge ? (pl.splits + kMergeGroup - 1) / kMergeGroup : 0;
     pl.rec_bytes = pl.splits > 1 ? (size_t)streams * (pl.splits + ngrp) * (40 + 8 * D) * sizeof(float) : 0;
     pl.ticket_bytes = 16 + (size_t)streams * (1 + ngrp) * sizeof(int32_t);
     pl.qproj_bytes = (size_t)sh->B * sh->Hq * 2 * D * sizeof(float);
