@@ -2317,9 +2317,11 @@ Plan make_cl_plan(const FkvDecodeShape* sh, bool turbo) {
 // range.  Chosen by default when a CTA's planned work is at least
 // kUmMinChunk cost units: on B200 the tensor-core path's CTAs start (TMEM
 // allocation, q pieces, first MMA) and drain about 3 us later while each far
-// token costs a few percent less (c3, ~19K units per CTA: 633 vs 611 us; c4,
-// ~61K per CTA: 312 vs 322 us).  FKV_QK_PATH=mma / tcgen05 forces either.
-constexpr int64_t kUmMinChunk = 40000;
+// token costs a few percent less, and it takes the two-level split merge
+// (c3, ~19K units per CTA: 633 vs 611 us; c4 2-GPU shards, ~30K per CTA:
+// 168.4 vs 175.9 us per step; 4-GPU shards, ~23K: 106.3 vs 102.2; c4 on one
+// GPU, ~61K: 312 vs 322 us).  FKV_QK_PATH=mma / tcgen05 forces either.
+constexpr int64_t kUmMinChunk = 27000;
 
 int um_heads(const FkvDecodeShape* sh, bool turbo) {
     if (turbo || sh->D != 128 || sh->n_far <= 0) return 0;
