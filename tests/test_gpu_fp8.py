@@ -218,7 +218,7 @@ def _raw_decode(lay, sh, q, Hq, D):
     return out, fl, tk
 
 
-@pytest.mark.parametrize("G,D,splits", [(1, 128, 13), (1, 128, 32), (2, 128, 16), (1, 64, 60),
+@pytest.mark.parametrize("G,D,splits", [(1, 128, 13), (1, 128, 32), (1, 128, 48), (2, 128, 16), (1, 64, 60), (2, 64, 60),
                                          (4, 64, 16)])
 def test_decode_few_heads_many_splits(G, D, splits, qk_path):
     """Streams with few q heads (G < 8) and more split records than the direct
