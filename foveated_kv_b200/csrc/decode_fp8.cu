@@ -650,16 +650,21 @@ __global__ void __launch_bounds__(kQpThreads)
                        const float* __restrict__ Sm, float* __restrict__ out, int BH) {
     __shared__ __align__(16) float mrow[kQpRows][D + 4];
     __shared__ __align__(16) float qv[kQpHeads][D + 4];
-    // the decode kernel launched next may start now: only its warp that reads
-    // these projections waits for this grid (griddepcontrol.wait)
-    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int o0 = blockIdx.x * kQpRows, h0 = blockIdx.y * kQpHeads;
     const int tid = threadIdx.x;
+    // Pi and S are constants: staged while the previous kernel of the stream
+    // may still run (this grid is launched with programmatic serialization)
     for (int i = tid; i < kQpRows * D / 4; i += kQpThreads) {
         const int r = i / (D / 4), c4 = i % (D / 4), o = o0 + r;
         const float* src = (o < D ? Pi + (int64_t)o * D : Sm + (int64_t)(o - D) * D) + 4 * c4;
         *reinterpret_cast<float4*>(&mrow[r][4 * c4]) = __ldg(reinterpret_cast<const float4*>(src));
     }
+    // q may be the previous kernel's output: wait for it to complete; then
+    // the decode kernel launched next may start (only its warp that reads
+    // these projections waits for this grid; its other reads are ordered
+    // after this grid's wait)
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     for (int i = tid; i < kQpHeads * D / 8; i += kQpThreads) {
         const int j = i / (D / 8), c8 = i % (D / 8);
         uint4 w = make_uint4(0, 0, 0, 0);
@@ -2475,10 +2480,22 @@ int launch(const FkvDecodeShape* sh, DecodeParams& p, void* workspace, size_t ws
         FKV_REQUIRE((BH + kQpHeads - 1) / kQpHeads <= 65535, FKV_ERR_UNSUPPORTED,
                     "B*Hq=%d exceeds the q-projection grid limit", BH);
         const dim3 qg(2 * sh->D / kQpRows, (BH + kQpHeads - 1) / kQpHeads);
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = qg;
+        cfg.blockDim = dim3(kQpThreads);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
         if (sh->D == 128)
-            turbo_qproj_kernel<128><<<qg, kQpThreads, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj, BH);
+            FKV_CUDA_CHECK(cudaLaunchKernelEx(&cfg, turbo_qproj_kernel<128>, p.q, p.turbo_pi, p.turbo_s,
+                                              qproj, BH));
         else
-            turbo_qproj_kernel<64><<<qg, kQpThreads, 0, st>>>(p.q, p.turbo_pi, p.turbo_s, qproj, BH);
+            FKV_CUDA_CHECK(cudaLaunchKernelEx(&cfg, turbo_qproj_kernel<64>, p.q, p.turbo_pi, p.turbo_s,
+                                              qproj, BH));
         FKV_LAUNCH_CHECK();
     }
     // Early start only for grids of at most one CTA per SM: their CTAs land
